@@ -1,0 +1,227 @@
+/*
+ * tcc_b200.h -- C ABI of the B200-native (sm_100a) tcc graph-aggregation path.
+ *
+ * Plain pointers, sizes and cudaStream_t only.  Every entry point names the
+ * reference interface it replaces (paths relative to the reference project
+ * root; "cnic/" is TAC_training_backend/spmm_cnic/).  All device pointers are
+ * global-memory pointers on the current device; calls are asynchronous on
+ * `stream` unless marked "synchronises".  No C++ exception crosses this ABI:
+ * each call returns a tcc_status and tcc_last_error() describes the last
+ * failure of the calling thread.
+ *
+ * Layouts are the reference's, bit for bit:
+ *   SWTCF  include/swtcf_convert.cuh:13-35 (8x8 tiles in 8-column windows,
+ *          16-window super-windows, 32-row repeat cache)
+ *   BCSR   cnic/include/class.h:20-37 (8-row windows, condensed columns)
+ *   BCSC   cnic/include/class.h:39-57 (8-column windows, condensed rows)
+ * with one canonical order where the reference's converter is order-free:
+ * rows of an SWTCF window by degree descending then dst ascending, super-window
+ * rows by dst ascending, cache ranks by occurrence descending then slot
+ * ascending; BCSR/BCSC condensed indices ascending, padding 0xFFFFFFFF.
+ */
+#ifndef TCC_B200_H
+#define TCC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------- status ---- */
+typedef int tcc_status;
+#define TCC_OK 0
+#define TCC_ERR_INVALID_ARGUMENT 1 /* reference: std::runtime_error("invalid ...") */
+#define TCC_ERR_CUDA 2             /* a CUDA runtime call failed */
+#define TCC_ERR_OUT_OF_MEMORY 3
+#define TCC_ERR_UNSUPPORTED 4      /* configuration the path does not implement */
+#define TCC_ERR_DEVICE 5           /* a kernel raised a device error code (below) */
+#define TCC_ERR_CAPACITY 6         /* output/workspace capacity too small */
+
+/* Device error codes written to a workspace error word (the reference's
+ * SWTCFConvertWorkspace::deviceError, src/swtcf_convert.cu:190-194, :582-585,
+ * :981-999, :765-775).  Codes 2 and 3 belong to the reference's hash table,
+ * which this implementation replaces by sorting; they are never raised. */
+#define TCC_DEVERR_NONE 0
+#define TCC_DEVERR_GROUP_DEGREE 1  /* a (window,row) group holds a duplicate edge */
+#define TCC_DEVERR_HASH_FULL 2
+#define TCC_DEVERR_HASH_LOOKUP 3
+#define TCC_DEVERR_OCCURRENCE 4    /* row occurrence above the super-window size */
+#define TCC_DEVERR_INDEX_RANGE 5   /* an input index >= rows/cols */
+
+const char* tcc_last_error(void);
+const char* tcc_version(void);
+
+/* ------------------------------------------------------------- SWTCF ----- */
+#define TCC_SWTCF_WINDOW 8
+#define TCC_SWTCF_CACHE_ROWS 32
+#define TCC_SWTCF_MAX_SUPER_WINDOW 32
+#define TCC_SWTCF_FEATURE_DIM 128      /* include/swtcf_spmm.cuh:7 */
+#define TCC_SWTCF_DEFAULT_TC_THRESHOLD 12
+
+/* Field-for-field DeviceSWTCFMatrix (include/swtcf_convert.cuh:13-35); the
+ * trailing fields are this implementation's. */
+typedef struct tcc_swtcf {
+    uint32_t rows, cols, nnz;
+    uint32_t colWindowWidth, tileRows, superWindowSize;
+    uint32_t numColWindows, numSuperWindows;
+    uint32_t* superWindowRowOffset;      /* [numSuperWindows+1] */
+    uint32_t* superWindowRows;           /* [capacity_rows] */
+    uint8_t* superWindowRowCacheSlot;    /* [capacity_rows], 0xFF = uncached */
+    uint32_t* superWindowCachedRowSlot;  /* [32*numSuperWindows] */
+    uint8_t* superWindowCachedCount;     /* [numSuperWindows] */
+    uint32_t* colWindowOffset;           /* [numColWindows+1] */
+    uint32_t* tileRowSlot;               /* [8*capacity_tiles], 0xFFFFFFFF = padding */
+    uint64_t* tileLocalBit;              /* [capacity_tiles], bit = localRow*8+localCol */
+    uint64_t capacity_tiles, capacity_rows;
+    /* work plan of the transposed pass, owned by the matrix; rebuilt lazily
+     * after each conversion */
+    void* pull_plan;
+    uint64_t pull_plan_bytes;
+    int32_t pull_plan_ready;
+} tcc_swtcf;
+
+typedef struct tcc_swtcf_workspace tcc_swtcf_workspace; /* opaque */
+
+/* allocateDeviceSWTCF (include/swtcf_convert.cuh:74; src/swtcf_convert.cu:1113-1263):
+ * capacities = nnz tiles / rows, like the reference. */
+tcc_status tcc_swtcf_alloc(tcc_swtcf* m, uint32_t rows, uint32_t cols, uint32_t nnz,
+                           uint32_t super_window_size);
+/* freeDeviceSWTCF (include/swtcf_convert.cuh:75) */
+tcc_status tcc_swtcf_free(tcc_swtcf* m);
+/* allocateSWTCFConvertWorkspace (include/swtcf_convert.cuh:76; src/swtcf_convert.cu:1306-1655) */
+tcc_status tcc_swtcf_workspace_create(tcc_swtcf_workspace** ws, uint64_t edge_capacity,
+                                      uint32_t num_src, uint32_t super_window_size);
+/* freeSWTCFConvertWorkspace (include/swtcf_convert.cuh:77) */
+tcc_status tcc_swtcf_workspace_destroy(tcc_swtcf_workspace* ws);
+/* convertCOOToSWTCF (include/swtcf_convert.cuh:78; src/swtcf_convert.cu:1754-2342):
+ * canonical, deterministic; device errors land in the workspace error word. */
+tcc_status tcc_swtcf_convert_coo(const uint32_t* d_dst, const uint32_t* d_src, uint64_t nnz,
+                                 tcc_swtcf* out, tcc_swtcf_workspace* ws, cudaStream_t stream);
+/* The CSR entry of the same conversion (row = dst, column = src). */
+tcc_status tcc_swtcf_convert_csr(const uint64_t* d_rowptr, const uint32_t* d_col,
+                                 uint32_t rows, uint64_t nnz, tcc_swtcf* out,
+                                 tcc_swtcf_workspace* ws, cudaStream_t stream);
+/* Reads the workspace's device error word (synchronises the stream). */
+tcc_status tcc_swtcf_workspace_device_error(tcc_swtcf_workspace* ws, cudaStream_t stream,
+                                            uint32_t* code);
+/* T = colWindowOffset[numColWindows], R = superWindowRowOffset[numSuperWindows]
+ * (synchronises the stream). */
+tcc_status tcc_swtcf_sizes(const tcc_swtcf* m, cudaStream_t stream, uint64_t* num_tiles,
+                           uint64_t* num_rows);
+
+/* launchSWTCFSpMM (include/swtcf_spmm.cuh:10-16; src/swtcf_spmm.cu:437-466):
+ * Y[numDst x 128] += pattern(A) * X[numSrc x 128]; tiles with popcount >=
+ * tc_threshold use TF32 tensor cores, the others fp32.  Requires
+ * superWindowSize == 16, like the reference. */
+tcc_status tcc_swtcf_spmm(const tcc_swtcf* m, const float* X, float* Y, uint32_t tc_threshold,
+                          cudaStream_t stream);
+/* General form: any F (multiple of 4), row strides, diagonal scales fused
+ * (Y = diag(row_scale) * A * diag(col_scale) * X, NULL = ones); accumulate = 0
+ * overwrites Y (the reference always accumulates). */
+tcc_status tcc_swtcf_spmm_ex(const tcc_swtcf* m, const float* X, uint64_t ldx, float* Y,
+                             uint64_t ldy, uint32_t F, uint32_t tc_threshold,
+                             const float* row_scale, const float* col_scale, int accumulate,
+                             cudaStream_t stream);
+/* Transposed pass over the same tiles: Z[numSrc x F] = diag(col_scale) * A^T *
+ * diag(row_scale) * G[numDst x F].  Owner-computes per column window: each
+ * output row is written once, except rows of windows with more than 32 tiles,
+ * which several warps reduce into. */
+tcc_status tcc_swtcf_spmm_t(const tcc_swtcf* m, const float* G, uint64_t ldg, float* Z,
+                            uint64_t ldz, uint32_t F, uint32_t tc_threshold,
+                            const float* row_scale, const float* col_scale, int accumulate,
+                            cudaStream_t stream);
+
+/* -------------------------------------------------------- BCSR / BCSC ---- */
+/* Field-for-field BCSR<float> (cnic/include/class.h:20-37). */
+typedef struct tcc_bcsr {
+    uint32_t num_rows, num_cols, nnz, num_TCBlocks, num_rowWindows;
+    uint32_t* rowWindowOffset; /* [num_rowWindows+1] */
+    uint32_t* tcOffset;        /* [num_TCBlocks+1] prefix of tile popcounts */
+    uint32_t* sparseA2B;       /* [8*num_TCBlocks] condensed columns, pad 0xFFFFFFFF */
+    uint64_t* tcLocalBit;      /* [num_TCBlocks] bit = row*8 + k */
+} tcc_bcsr;
+
+/* Field-for-field BCSC<float> (cnic/include/class.h:39-57). */
+typedef struct tcc_bcsc {
+    uint32_t num_rows, num_cols, nnz, num_TCBlocks, num_colWindows;
+    uint32_t* colWindowOffset; /* [num_colWindows+1] */
+    uint32_t* tcOffset;        /* [num_TCBlocks+1] */
+    uint32_t* sparseA2C;       /* [8*num_TCBlocks] condensed rows, pad 0xFFFFFFFF */
+    uint64_t* tcLocalBit;      /* [num_TCBlocks] bit = n*8 + k */
+} tcc_bcsc;
+
+typedef struct tcc_tiles_workspace tcc_tiles_workspace; /* opaque */
+
+#define TCC_TILES_BCSR 0
+#define TCC_TILES_BCSC 1
+
+/* CSR -> BCSR / BCSC window tiling on the GPU (the producer the reference
+ * leaves to its absent sampler, train/tcgnn_conv_release.py:284-301), two steps:
+ * prepare (sort + group; synchronises to return the tile count T) then fill
+ * the caller's arrays (sized from T). */
+tcc_status tcc_tiles_workspace_create(tcc_tiles_workspace** ws, uint64_t nnz_capacity,
+                                      uint32_t rows, uint32_t cols);
+tcc_status tcc_tiles_workspace_destroy(tcc_tiles_workspace* ws);
+tcc_status tcc_tiles_prepare_csr(tcc_tiles_workspace* ws, int kind, const uint64_t* d_rowptr,
+                                 const uint32_t* d_col, uint32_t rows, uint32_t cols,
+                                 uint64_t nnz, cudaStream_t stream, uint64_t* num_tiles);
+tcc_status tcc_tiles_fill_bcsr(tcc_tiles_workspace* ws, tcc_bcsr* out, cudaStream_t stream);
+tcc_status tcc_tiles_fill_bcsc(tcc_tiles_workspace* ws, tcc_bcsc* out, cudaStream_t stream);
+
+/* Pull-SpMM scratch (the window->chunk work plan): bytes needed for a tiling
+ * with `num_windows` windows and `num_tiles` tiles.  The scratch belongs to the
+ * caller; pass plan_ready = 1 to reuse a plan built by an earlier call on the
+ * same tiling. */
+size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
+
+/* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
+ * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):
+ * C[num_rows x F] = diag(rs) * A * diag(cs) * B[num_cols x F]; row windows own
+ * their outputs (no atomics except for windows split across warps). */
+tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float* C,
+                         uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
+                         const float* cs, int accumulate, void* scratch, size_t scratch_bytes,
+                         int plan_ready, cudaStream_t stream);
+/* tf32_spmm_bcsc + tf32_computeX128TransposePipe2_BCSC
+ * (cnic/src/core/spmm_dispatcher.cu:235-302, spmm_kernel.cu:1844-2167): the
+ * column-window push pass, C += diag(rs) * A * diag(cs) * B, accumulated with
+ * vector fp32 reductions (the reference accumulates with atomics too). */
+tcc_status tcc_bcsc_spmm(const tcc_bcsc* a, const float* B, uint64_t ldb, float* C,
+                         uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
+                         const float* cs, cudaStream_t stream);
+/* The transposed (backward) pass over BCSC tiles: Z[num_cols x F] =
+ * diag(cs) * A^T * diag(rs) * G[num_rows x F], owner-computes per column
+ * window.  Replaces torch.sparse.mm(A_topo.T, d_output) of
+ * train/tcgnn_conv_release.py:150-154. */
+tcc_status tcc_bcsc_spmm_t(const tcc_bcsc* a, const float* G, uint64_t ldg, float* Z,
+                           uint64_t ldz, uint32_t F, uint32_t tc_threshold, const float* rs,
+                           const float* cs, int accumulate, void* scratch,
+                           size_t scratch_bytes, int plan_ready, cudaStream_t stream);
+/* launch_spmm_kernel, non-mixed (cnic/src/core/spmm_launcher.cu:203-271):
+ * C[(num_rowWindows+1)*8 x F] = BCSR*B + BCSC*B (either may be NULL).  The
+ * reference memsets C and atomically adds both passes; here the BCSR pass
+ * stores and the BCSC pass reduces after it, on one stream.  tc_threshold 0
+ * reproduces the reference's TF32-on-every-tile arithmetic. */
+tcc_status tcc_cnic_forward(const tcc_bcsr* bcsr, const tcc_bcsc* bcsc, const float* B,
+                            float* C, uint32_t F, uint32_t tc_threshold, void* scratch,
+                            size_t scratch_bytes, cudaStream_t stream);
+/* launch_spmm_kernel, mixed (cnic/src/core/spmm_launcher.cu:115-200,
+ * spmm_kernel.cu:129-153): the B row of condensed column c comes from the
+ * feature store: g = cache_search_map[c] >= 0 -> gpu_features[g / gpu_capacity]
+ * + (g % gpu_capacity) * F (device pointers, an array in device memory); else
+ * cpu_features + id_map[c] * F (pinned host memory mapped into the device
+ * address space).  Hot rows are read from HBM, cold rows over the host link. */
+tcc_status tcc_cnic_forward_mixed(const tcc_bcsr* bcsr, const tcc_bcsc* bcsc,
+                                  const int32_t* id_map, const float* cpu_features,
+                                  const int32_t* cache_search_map,
+                                  const float* const* gpu_features, int64_t gpu_capacity,
+                                  float* C, uint32_t F, uint32_t tc_threshold, void* scratch,
+                                  size_t scratch_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TCC_B200_H */

@@ -1,0 +1,125 @@
+"""ctypes binding of tcc_b200/libtcc_b200.so (the C ABI of include/tcc_b200.h).
+
+There is no fallback: if the library is missing or cannot be loaded, every
+entry point raises.  Build it with ``python -m tcc_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtcc_b200.so")
+
+TCC_OK = 0
+STATUS_NAMES = {0: "TCC_OK", 1: "TCC_ERR_INVALID_ARGUMENT", 2: "TCC_ERR_CUDA",
+                3: "TCC_ERR_OUT_OF_MEMORY", 4: "TCC_ERR_UNSUPPORTED", 5: "TCC_ERR_DEVICE",
+                6: "TCC_ERR_CAPACITY"}
+TILES_BCSR = 0
+TILES_BCSC = 1
+DEVERR_GROUP_DEGREE = 1
+DEVERR_INDEX_RANGE = 5
+
+
+class TccError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class Swtcf(C.Structure):
+    """Field-for-field tcc_swtcf / the reference's DeviceSWTCFMatrix."""
+    _fields_ = [("rows", C.c_uint32), ("cols", C.c_uint32), ("nnz", C.c_uint32),
+                ("colWindowWidth", C.c_uint32), ("tileRows", C.c_uint32),
+                ("superWindowSize", C.c_uint32), ("numColWindows", C.c_uint32),
+                ("numSuperWindows", C.c_uint32),
+                ("superWindowRowOffset", C.c_void_p), ("superWindowRows", C.c_void_p),
+                ("superWindowRowCacheSlot", C.c_void_p), ("superWindowCachedRowSlot", C.c_void_p),
+                ("superWindowCachedCount", C.c_void_p), ("colWindowOffset", C.c_void_p),
+                ("tileRowSlot", C.c_void_p), ("tileLocalBit", C.c_void_p),
+                ("capacity_tiles", C.c_uint64), ("capacity_rows", C.c_uint64),
+                ("pull_plan", C.c_void_p), ("pull_plan_bytes", C.c_uint64),
+                ("pull_plan_ready", C.c_int32)]
+
+
+class Bcsr(C.Structure):
+    """Field-for-field tcc_bcsr / the reference's BCSR<float>."""
+    _fields_ = [("num_rows", C.c_uint32), ("num_cols", C.c_uint32), ("nnz", C.c_uint32),
+                ("num_TCBlocks", C.c_uint32), ("num_rowWindows", C.c_uint32),
+                ("rowWindowOffset", C.c_void_p), ("tcOffset", C.c_void_p),
+                ("sparseA2B", C.c_void_p), ("tcLocalBit", C.c_void_p)]
+
+
+class Bcsc(C.Structure):
+    """Field-for-field tcc_bcsc / the reference's BCSC<float>."""
+    _fields_ = [("num_rows", C.c_uint32), ("num_cols", C.c_uint32), ("nnz", C.c_uint32),
+                ("num_TCBlocks", C.c_uint32), ("num_colWindows", C.c_uint32),
+                ("colWindowOffset", C.c_void_p), ("tcOffset", C.c_void_p),
+                ("sparseA2C", C.c_void_p), ("tcLocalBit", C.c_void_p)]
+
+
+# name -> (restype, argtypes); the symbols include/tcc_b200.h declares
+_vp = C.c_void_p
+_u32 = C.c_uint32
+_u64 = C.c_uint64
+_i = C.c_int
+_st = C.c_int
+PROTOTYPES = {
+    "tcc_last_error": (C.c_char_p, []),
+    "tcc_version": (C.c_char_p, []),
+    "tcc_swtcf_alloc": (_st, [C.POINTER(Swtcf), _u32, _u32, _u32, _u32]),
+    "tcc_swtcf_free": (_st, [C.POINTER(Swtcf)]),
+    "tcc_swtcf_workspace_create": (_st, [C.POINTER(_vp), _u64, _u32, _u32]),
+    "tcc_swtcf_workspace_destroy": (_st, [_vp]),
+    "tcc_swtcf_convert_coo": (_st, [_vp, _vp, _u64, C.POINTER(Swtcf), _vp, _vp]),
+    "tcc_swtcf_convert_csr": (_st, [_vp, _vp, _u32, _u64, C.POINTER(Swtcf), _vp, _vp]),
+    "tcc_swtcf_workspace_device_error": (_st, [_vp, _vp, C.POINTER(_u32)]),
+    "tcc_swtcf_sizes": (_st, [C.POINTER(Swtcf), _vp, C.POINTER(_u64), C.POINTER(_u64)]),
+    "tcc_swtcf_spmm": (_st, [C.POINTER(Swtcf), _vp, _vp, _u32, _vp]),
+    "tcc_swtcf_spmm_ex": (_st, [C.POINTER(Swtcf), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
+                                _i, _vp]),
+    "tcc_swtcf_spmm_t": (_st, [C.POINTER(Swtcf), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i,
+                               _vp]),
+    "tcc_tiles_workspace_create": (_st, [C.POINTER(_vp), _u64, _u32, _u32]),
+    "tcc_tiles_workspace_destroy": (_st, [_vp]),
+    "tcc_tiles_prepare_csr": (_st, [_vp, _i, _vp, _vp, _u32, _u32, _u64, _vp, C.POINTER(_u64)]),
+    "tcc_tiles_fill_bcsr": (_st, [_vp, C.POINTER(Bcsr), _vp]),
+    "tcc_tiles_fill_bcsc": (_st, [_vp, C.POINTER(Bcsc), _vp]),
+    "tcc_pull_scratch_bytes": (C.c_size_t, [_u32, _u32]),
+    "tcc_bcsr_spmm": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i, _vp,
+                            C.c_size_t, _i, _vp]),
+    "tcc_bcsc_spmm": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),
+    "tcc_bcsc_spmm_t": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i,
+                              _vp, C.c_size_t, _i, _vp]),
+    "tcc_cnic_forward": (_st, [C.POINTER(Bcsr), C.POINTER(Bcsc), _vp, _vp, _u32, _u32, _vp,
+                               C.c_size_t, _vp]),
+    "tcc_cnic_forward_mixed": (_st, [C.POINTER(Bcsr), C.POINTER(Bcsc), _vp, _vp, _vp, _vp,
+                                     C.c_int64, _vp, _u32, _u32, _vp, C.c_size_t, _vp]),
+}
+
+_LIB = None
+
+
+def lib():
+    """The loaded library; raises if it is absent (no CPU fallback exists)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise TccError(-1, f"{LIB_PATH} is missing; build it with `python -m tcc_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in PROTOTYPES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def check(status: int, what: str = ""):
+    if status != TCC_OK:
+        msg = lib().tcc_last_error().decode(errors="replace")
+        raise TccError(status, f"{what}: {msg}" if what else msg)
+
+
+def call(name: str, *args):
+    check(getattr(lib(), name)(*args), name)

@@ -1,0 +1,432 @@
+// capi.cu -- the extern "C" boundary (include/tcc_b200.h) over the sm_100a
+// kernels.  Exceptions never cross it: every entry point returns a tcc_status
+// and records a message for tcc_last_error().
+#include "convert.cuh"
+#include "spmm.cuh"
+
+#include <string>
+
+struct tcc_swtcf_workspace {
+    tcc::SwtcfWorkspace impl;
+    tcc_swtcf_workspace(uint64_t e, uint32_t n, uint32_t s) : impl(e, n, s) {}
+};
+struct tcc_tiles_workspace {
+    tcc::TilesWorkspace impl;
+    tcc_tiles_workspace(uint64_t e, uint32_t r, uint32_t c) : impl(e, r, c) {}
+};
+
+namespace {
+thread_local std::string g_last_error;
+
+template <typename Fn>
+tcc_status guarded(const char* where, Fn&& fn) {
+    try {
+        fn();
+        return TCC_OK;
+    } catch (const tcc::Error& e) {
+        g_last_error = std::string(where) + ": " + e.what();
+        return e.status;
+    } catch (const std::bad_alloc&) {
+        g_last_error = std::string(where) + ": host out of memory";
+        return TCC_ERR_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        g_last_error = std::string(where) + ": " + e.what();
+        return TCC_ERR_INVALID_ARGUMENT;
+    }
+}
+
+template <typename T>
+void dev_alloc(T** p, uint64_t n) {
+    *p = nullptr;
+    TCC_CUDA(cudaMalloc(reinterpret_cast<void**>(p), std::max<uint64_t>(n, 1) * sizeof(T)));
+}
+
+void zero_rows(float* Y, uint64_t ldy, uint32_t F, uint64_t rows, cudaStream_t s) {
+    if (!rows) return;
+    if (ldy == F) TCC_CUDA(cudaMemsetAsync(Y, 0, rows * F * sizeof(float), s));
+    else TCC_CUDA(cudaMemset2DAsync(Y, ldy * sizeof(float), 0, F * sizeof(float), rows, s));
+}
+
+tcc::PullTiles bcsr_pull(const tcc_bcsr* a) {
+    tcc::PullTiles t{};
+    t.num_windows = a->num_rowWindows;
+    t.num_tiles = a->num_TCBlocks;
+    t.win_offset = a->rowWindowOffset;
+    t.bits = a->tcLocalBit;
+    t.idx = a->sparseA2B;
+    t.bits_transposed = false;
+    t.num_out = a->num_rows;
+    t.num_in = a->num_cols;
+    return t;
+}
+
+tcc::PullTiles bcsc_pull_t(const tcc_bcsc* a) {
+    tcc::PullTiles t{};
+    t.num_windows = a->num_colWindows;
+    t.num_tiles = a->num_TCBlocks;
+    t.win_offset = a->colWindowOffset;
+    t.bits = a->tcLocalBit;
+    t.idx = a->sparseA2C;
+    t.bits_transposed = true;
+    t.num_out = a->num_cols;
+    t.num_in = a->num_rows;
+    return t;
+}
+
+tcc::PushTiles bcsc_push(const tcc_bcsc* a) {
+    tcc::PushTiles t{};
+    t.num_windows = a->num_colWindows;
+    t.win_offset = a->colWindowOffset;
+    t.bits = a->tcLocalBit;
+    t.idx = a->sparseA2C;
+    t.num_out = a->num_rows;
+    t.num_in = a->num_cols;
+    return t;
+}
+
+void check_bcsr(const tcc_bcsr* a) {
+    TCC_REQUIRE(a && a->rowWindowOffset && a->tcLocalBit && a->sparseA2B, "BCSR arrays missing");
+    TCC_REQUIRE(a->num_rowWindows == (a->num_rows + 7) / 8, "num_rowWindows != ceil(num_rows/8)");
+}
+void check_bcsc(const tcc_bcsc* a) {
+    TCC_REQUIRE(a && a->colWindowOffset && a->tcLocalBit && a->sparseA2C, "BCSC arrays missing");
+    TCC_REQUIRE(a->num_colWindows == (a->num_cols + 7) / 8, "num_colWindows != ceil(num_cols/8)");
+}
+}  // namespace
+
+extern "C" {
+
+const char* tcc_last_error(void) { return g_last_error.c_str(); }
+const char* tcc_version(void) { return "tcc_b200 0.1 (sm_100a)"; }
+
+// ------------------------------------------------------------------- SWTCF --
+
+tcc_status tcc_swtcf_alloc(tcc_swtcf* m, uint32_t rows, uint32_t cols, uint32_t nnz,
+                           uint32_t S) {
+    return guarded("tcc_swtcf_alloc", [&] {
+        TCC_REQUIRE(m, "null matrix");
+        TCC_REQUIRE(cols > 0 && nnz > 0 && S > 0 && S <= TCC_SWTCF_MAX_SUPER_WINDOW,
+                    "invalid SWTCF allocation size");
+        *m = tcc_swtcf{};
+        m->rows = rows;
+        m->cols = cols;
+        m->nnz = nnz;
+        m->colWindowWidth = 8;
+        m->tileRows = 8;
+        m->superWindowSize = S;
+        m->numColWindows = (cols + 7) / 8;
+        m->numSuperWindows = (m->numColWindows + S - 1) / S;
+        m->capacity_tiles = nnz;
+        m->capacity_rows = nnz;
+        try {
+            dev_alloc(&m->superWindowRowOffset, (uint64_t)m->numSuperWindows + 1);
+            dev_alloc(&m->superWindowRows, nnz);
+            dev_alloc(&m->superWindowRowCacheSlot, nnz);
+            dev_alloc(&m->superWindowCachedRowSlot, (uint64_t)m->numSuperWindows * 32);
+            dev_alloc(&m->superWindowCachedCount, m->numSuperWindows);
+            dev_alloc(&m->colWindowOffset, (uint64_t)m->numColWindows + 1);
+            dev_alloc(&m->tileRowSlot, (uint64_t)nnz * 8);
+            dev_alloc(&m->tileLocalBit, nnz);
+            m->pull_plan_bytes = tcc::pull_scratch_bytes(m->numColWindows, nnz);
+            TCC_CUDA(cudaMalloc(&m->pull_plan, m->pull_plan_bytes));
+        } catch (...) {
+            tcc_swtcf_free(m);
+            throw;
+        }
+    });
+}
+
+tcc_status tcc_swtcf_free(tcc_swtcf* m) {
+    return guarded("tcc_swtcf_free", [&] {
+        if (!m) return;
+        cudaFree(m->superWindowRowOffset);
+        cudaFree(m->superWindowRows);
+        cudaFree(m->superWindowRowCacheSlot);
+        cudaFree(m->superWindowCachedRowSlot);
+        cudaFree(m->superWindowCachedCount);
+        cudaFree(m->colWindowOffset);
+        cudaFree(m->tileRowSlot);
+        cudaFree(m->tileLocalBit);
+        cudaFree(m->pull_plan);
+        *m = tcc_swtcf{};
+    });
+}
+
+tcc_status tcc_swtcf_workspace_create(tcc_swtcf_workspace** ws, uint64_t edge_capacity,
+                                      uint32_t num_src, uint32_t S) {
+    return guarded("tcc_swtcf_workspace_create", [&] {
+        TCC_REQUIRE(ws, "null workspace pointer");
+        *ws = nullptr;
+        TCC_REQUIRE(edge_capacity > 0 && num_src > 0 && S > 0 && S <= TCC_SWTCF_MAX_SUPER_WINDOW,
+                    "invalid converter workspace size");
+        TCC_REQUIRE(edge_capacity < (1ull << 31), "edge capacity must stay below 2^31");
+        *ws = new tcc_swtcf_workspace(edge_capacity, num_src, S);
+    });
+}
+
+tcc_status tcc_swtcf_workspace_destroy(tcc_swtcf_workspace* ws) {
+    return guarded("tcc_swtcf_workspace_destroy", [&] { delete ws; });
+}
+
+tcc_status tcc_swtcf_convert_coo(const uint32_t* d_dst, const uint32_t* d_src, uint64_t nnz,
+                                 tcc_swtcf* out, tcc_swtcf_workspace* ws, cudaStream_t stream) {
+    return guarded("tcc_swtcf_convert_coo", [&] {
+        TCC_REQUIRE(ws && out && d_dst && d_src, "null argument");
+        tcc::swtcf_convert(d_dst, d_src, nullptr, nullptr, nnz, out, ws->impl, stream);
+        out->pull_plan_ready = 0;
+    });
+}
+
+tcc_status tcc_swtcf_convert_csr(const uint64_t* d_rowptr, const uint32_t* d_col, uint32_t rows,
+                                 uint64_t nnz, tcc_swtcf* out, tcc_swtcf_workspace* ws,
+                                 cudaStream_t stream) {
+    return guarded("tcc_swtcf_convert_csr", [&] {
+        TCC_REQUIRE(ws && out && d_rowptr && d_col, "null argument");
+        TCC_REQUIRE(rows == out->rows, "CSR row count differs from the matrix's rows");
+        tcc::swtcf_convert(nullptr, nullptr, d_rowptr, d_col, nnz, out, ws->impl, stream);
+        out->pull_plan_ready = 0;
+    });
+}
+
+tcc_status tcc_swtcf_workspace_device_error(tcc_swtcf_workspace* ws, cudaStream_t stream,
+                                            uint32_t* code) {
+    return guarded("tcc_swtcf_workspace_device_error", [&] {
+        TCC_REQUIRE(ws && code, "null argument");
+        TCC_CUDA(cudaMemcpyAsync(code, ws->impl.small, 4, cudaMemcpyDeviceToHost, stream));
+        TCC_CUDA(cudaStreamSynchronize(stream));
+    });
+}
+
+tcc_status tcc_swtcf_sizes(const tcc_swtcf* m, cudaStream_t stream, uint64_t* num_tiles,
+                           uint64_t* num_rows) {
+    return guarded("tcc_swtcf_sizes", [&] {
+        TCC_REQUIRE(m && num_tiles && num_rows, "null argument");
+        uint32_t t = 0, r = 0;
+        TCC_CUDA(cudaMemcpyAsync(&t, m->colWindowOffset + m->numColWindows, 4,
+                                 cudaMemcpyDeviceToHost, stream));
+        TCC_CUDA(cudaMemcpyAsync(&r, m->superWindowRowOffset + m->numSuperWindows, 4,
+                                 cudaMemcpyDeviceToHost, stream));
+        TCC_CUDA(cudaStreamSynchronize(stream));
+        *num_tiles = t;
+        *num_rows = r;
+    });
+}
+
+static tcc::PushTiles swtcf_push(const tcc_swtcf* m) {
+    tcc::PushTiles t{};
+    t.num_windows = m->numColWindows;
+    t.win_offset = m->colWindowOffset;
+    t.bits = m->tileLocalBit;
+    t.idx = m->tileRowSlot;
+    t.sw_offset = m->superWindowRowOffset;
+    t.sw_rows = m->superWindowRows;
+    t.sw_cache_slot = m->superWindowRowCacheSlot;
+    t.sw_cached_row_slot = m->superWindowCachedRowSlot;
+    t.sw_cached_count = m->superWindowCachedCount;
+    t.S = m->superWindowSize;
+    t.num_out = m->rows;
+    t.num_in = m->cols;
+    return t;
+}
+
+tcc_status tcc_swtcf_spmm(const tcc_swtcf* m, const float* X, float* Y, uint32_t tc_threshold,
+                          cudaStream_t stream) {
+    return guarded("tcc_swtcf_spmm", [&] {
+        TCC_REQUIRE(m && X && Y, "null argument");
+        TCC_REQUIRE(m->superWindowSize == 16, "SWTCF SpMM requires superWindowSize=16");
+        tcc::Dense d{X, 128, Y, 128, 128, nullptr, nullptr};
+        tcc::push_spmm(swtcf_push(m), d, tc_threshold, nullptr, stream);
+    });
+}
+
+tcc_status tcc_swtcf_spmm_ex(const tcc_swtcf* m, const float* X, uint64_t ldx, float* Y,
+                             uint64_t ldy, uint32_t F, uint32_t tc_threshold,
+                             const float* row_scale, const float* col_scale, int accumulate,
+                             cudaStream_t stream) {
+    return guarded("tcc_swtcf_spmm_ex", [&] {
+        TCC_REQUIRE(m && X && Y, "null argument");
+        if (!accumulate) zero_rows(Y, ldy, F, m->rows, stream);
+        tcc::Dense d{X, ldx, Y, ldy, F, row_scale, col_scale};
+        tcc::push_spmm(swtcf_push(m), d, tc_threshold, nullptr, stream);
+    });
+}
+
+tcc_status tcc_swtcf_spmm_t(const tcc_swtcf* m, const float* G, uint64_t ldg, float* Z,
+                            uint64_t ldz, uint32_t F, uint32_t tc_threshold,
+                            const float* row_scale, const float* col_scale, int accumulate,
+                            cudaStream_t stream) {
+    return guarded("tcc_swtcf_spmm_t", [&] {
+        TCC_REQUIRE(m && G && Z, "null argument");
+        tcc::PullTiles t{};
+        t.num_windows = m->numColWindows;
+        t.num_tiles = (uint32_t)m->capacity_tiles;
+        t.win_offset = m->colWindowOffset;
+        t.bits = m->tileLocalBit;
+        t.idx = m->tileRowSlot;
+        t.bits_transposed = true;
+        t.sw_offset = m->superWindowRowOffset;
+        t.sw_rows = m->superWindowRows;
+        t.S = m->superWindowSize;
+        t.num_out = m->cols;
+        t.num_in = m->rows;
+        // Z = diag(cs) A^T diag(rs) G: G rows are scaled by rs, Z rows by cs
+        tcc::Dense d{G, ldg, Z, ldz, F, col_scale, row_scale};
+        tcc::pull_spmm(t, d, tc_threshold, accumulate, m->pull_plan, m->pull_plan_bytes,
+                       m->pull_plan_ready != 0, nullptr, stream);
+        const_cast<tcc_swtcf*>(m)->pull_plan_ready = 1;
+    });
+}
+
+// -------------------------------------------------------------- BCSR/BCSC --
+
+tcc_status tcc_tiles_workspace_create(tcc_tiles_workspace** ws, uint64_t nnz_capacity,
+                                      uint32_t rows, uint32_t cols) {
+    return guarded("tcc_tiles_workspace_create", [&] {
+        TCC_REQUIRE(ws, "null workspace pointer");
+        *ws = nullptr;
+        TCC_REQUIRE(rows > 0 && cols > 0, "empty matrix shape");
+        TCC_REQUIRE(nnz_capacity < (1ull << 31), "nnz capacity must stay below 2^31");
+        *ws = new tcc_tiles_workspace(nnz_capacity, rows, cols);
+    });
+}
+
+tcc_status tcc_tiles_workspace_destroy(tcc_tiles_workspace* ws) {
+    return guarded("tcc_tiles_workspace_destroy", [&] { delete ws; });
+}
+
+tcc_status tcc_tiles_prepare_csr(tcc_tiles_workspace* ws, int kind, const uint64_t* d_rowptr,
+                                 const uint32_t* d_col, uint32_t rows, uint32_t cols,
+                                 uint64_t nnz, cudaStream_t stream, uint64_t* num_tiles) {
+    return guarded("tcc_tiles_prepare_csr", [&] {
+        TCC_REQUIRE(ws && d_rowptr && num_tiles && (d_col || nnz == 0), "null argument");
+        *num_tiles = tcc::tiles_prepare(ws->impl, kind, d_rowptr, d_col, rows, cols, nnz, stream);
+    });
+}
+
+tcc_status tcc_tiles_fill_bcsr(tcc_tiles_workspace* ws, tcc_bcsr* out, cudaStream_t stream) {
+    return guarded("tcc_tiles_fill_bcsr", [&] {
+        TCC_REQUIRE(ws && out, "null argument");
+        auto& w = ws->impl;
+        TCC_REQUIRE(out->rowWindowOffset && out->tcOffset && (w.T == 0 || (out->sparseA2B && out->tcLocalBit)),
+                    "BCSR arrays missing");
+        tcc::tiles_fill(w, TCC_TILES_BCSR, out->rowWindowOffset, out->tcOffset, out->sparseA2B,
+                        out->tcLocalBit, stream);
+        out->num_rows = w.cur_rows;
+        out->num_cols = w.cur_cols;
+        out->nnz = (uint32_t)w.nnz;
+        out->num_TCBlocks = (uint32_t)w.T;
+        out->num_rowWindows = w.W;
+    });
+}
+
+tcc_status tcc_tiles_fill_bcsc(tcc_tiles_workspace* ws, tcc_bcsc* out, cudaStream_t stream) {
+    return guarded("tcc_tiles_fill_bcsc", [&] {
+        TCC_REQUIRE(ws && out, "null argument");
+        auto& w = ws->impl;
+        TCC_REQUIRE(out->colWindowOffset && out->tcOffset && (w.T == 0 || (out->sparseA2C && out->tcLocalBit)),
+                    "BCSC arrays missing");
+        tcc::tiles_fill(w, TCC_TILES_BCSC, out->colWindowOffset, out->tcOffset, out->sparseA2C,
+                        out->tcLocalBit, stream);
+        out->num_rows = w.cur_rows;
+        out->num_cols = w.cur_cols;
+        out->nnz = (uint32_t)w.nnz;
+        out->num_TCBlocks = (uint32_t)w.T;
+        out->num_colWindows = w.W;
+    });
+}
+
+size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
+    return tcc::pull_scratch_bytes(num_windows, num_tiles);
+}
+
+tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float* C, uint64_t ldc,
+                         uint32_t F, uint32_t tc_threshold, const float* rs, const float* cs,
+                         int accumulate, void* scratch, size_t scratch_bytes, int plan_ready,
+                         cudaStream_t stream) {
+    return guarded("tcc_bcsr_spmm", [&] {
+        check_bcsr(a);
+        TCC_REQUIRE(B && C, "null argument");
+        tcc::Dense d{B, ldb, C, ldc, F, rs, cs};
+        tcc::pull_spmm(bcsr_pull(a), d, tc_threshold, accumulate, scratch, scratch_bytes,
+                       plan_ready != 0, nullptr, stream);
+    });
+}
+
+tcc_status tcc_bcsc_spmm(const tcc_bcsc* a, const float* B, uint64_t ldb, float* C, uint64_t ldc,
+                         uint32_t F, uint32_t tc_threshold, const float* rs, const float* cs,
+                         cudaStream_t stream) {
+    return guarded("tcc_bcsc_spmm", [&] {
+        check_bcsc(a);
+        TCC_REQUIRE(B && C, "null argument");
+        tcc::Dense d{B, ldb, C, ldc, F, rs, cs};
+        tcc::push_spmm(bcsc_push(a), d, tc_threshold, nullptr, stream);
+    });
+}
+
+tcc_status tcc_bcsc_spmm_t(const tcc_bcsc* a, const float* G, uint64_t ldg, float* Z,
+                           uint64_t ldz, uint32_t F, uint32_t tc_threshold, const float* rs,
+                           const float* cs, int accumulate, void* scratch, size_t scratch_bytes,
+                           int plan_ready, cudaStream_t stream) {
+    return guarded("tcc_bcsc_spmm_t", [&] {
+        check_bcsc(a);
+        TCC_REQUIRE(G && Z, "null argument");
+        tcc::Dense d{G, ldg, Z, ldz, F, cs, rs};
+        tcc::pull_spmm(bcsc_pull_t(a), d, tc_threshold, accumulate, scratch, scratch_bytes,
+                       plan_ready != 0, nullptr, stream);
+    });
+}
+
+static void cnic_forward(const tcc_bcsr* bcsr, const tcc_bcsc* bcsc, const float* B, float* C,
+                         uint32_t F, uint32_t thr, void* scratch, size_t scratch_bytes,
+                         const tcc::FeatureStore* fs, cudaStream_t stream) {
+    TCC_REQUIRE(bcsr || bcsc, "need a BCSR or a BCSC part");
+    TCC_REQUIRE(C && (fs || B), "null argument");
+    if (bcsr) check_bcsr(bcsr);
+    if (bcsc) check_bcsc(bcsc);
+    const uint32_t rows = bcsr ? bcsr->num_rows : bcsc->num_rows;
+    const uint32_t cols = bcsr ? bcsr->num_cols : bcsc->num_cols;
+    TCC_REQUIRE(!bcsr || !bcsc || (bcsr->num_rows == bcsc->num_rows && bcsr->num_cols == bcsc->num_cols),
+                "BCSR and BCSC parts disagree on the matrix shape");
+    const uint64_t padded = ((uint64_t)(rows + 7) / 8 + 1) * 8;  // spmm_launcher.cu:231
+    if (bcsr) {
+        tcc::Dense d{B, F, C, F, F, nullptr, nullptr};
+        tcc::pull_spmm(bcsr_pull(bcsr), d, thr, 0, scratch, scratch_bytes, false, fs, stream);
+        zero_rows(C + (uint64_t)rows * F, F, F, padded - rows, stream);
+    } else {
+        zero_rows(C, F, F, padded, stream);
+    }
+    (void)cols;
+    if (bcsc) {
+        tcc::Dense d{B, F, C, F, F, nullptr, nullptr};
+        tcc::push_spmm(bcsc_push(bcsc), d, thr, fs, stream);
+    }
+}
+
+tcc_status tcc_cnic_forward(const tcc_bcsr* bcsr, const tcc_bcsc* bcsc, const float* B, float* C,
+                            uint32_t F, uint32_t tc_threshold, void* scratch, size_t scratch_bytes,
+                            cudaStream_t stream) {
+    return guarded("tcc_cnic_forward", [&] {
+        cnic_forward(bcsr, bcsc, B, C, F, tc_threshold, scratch, scratch_bytes, nullptr, stream);
+    });
+}
+
+tcc_status tcc_cnic_forward_mixed(const tcc_bcsr* bcsr, const tcc_bcsc* bcsc,
+                                  const int32_t* id_map, const float* cpu_features,
+                                  const int32_t* cache_search_map,
+                                  const float* const* gpu_features, int64_t gpu_capacity,
+                                  float* C, uint32_t F, uint32_t tc_threshold, void* scratch,
+                                  size_t scratch_bytes, cudaStream_t stream) {
+    return guarded("tcc_cnic_forward_mixed", [&] {
+        TCC_REQUIRE(id_map && cache_search_map && cpu_features, "null feature-store argument");
+        TCC_REQUIRE(gpu_capacity > 0 && gpu_features, "GPU feature cache missing");
+        tcc::FeatureStore fs;
+        fs.id_map = id_map;
+        fs.cpu_features = cpu_features;
+        fs.cache_search_map = cache_search_map;
+        fs.gpu_features = gpu_features;
+        fs.gpu_capacity = gpu_capacity;
+        cnic_forward(bcsr, bcsc, nullptr, C, F, tc_threshold, scratch, scratch_bytes, &fs, stream);
+    });
+}
+
+}  // extern "C"

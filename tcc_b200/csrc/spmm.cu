@@ -1,0 +1,514 @@
+// spmm.cu -- SpMM over 8x8 window tiles on sm_100a.
+//
+// Pull (owner-computes) pass: one warp per chunk of <= kChunkTiles tiles of a
+// window; the window owns its 8 output rows, so rows are written once with
+// plain 16-byte stores (windows split into several chunks reduce with
+// red.global.add.v4.f32).  Per tile the 8 gather rows are loaded as coalesced
+// 128-bit lanes; tiles whose popcount reaches tc_threshold go through TF32
+// mma.sync m16n8k8 (the reference's arithmetic for dense tiles,
+// src/swtcf_spmm.cu:186-214, cnic/src/core/spmm_kernel.cu:1783-1801), the
+// others through fp32 FMA lanes.  Used for BCSR forward (cnic BCSR kernel,
+// spmm_kernel.cu:1560-1843) and for the transposed passes over BCSC / SWTCF
+// tiles, which replace torch.sparse.mm(A_topo.T, .) (train/tcgnn_conv_release.py:152).
+//
+// Push pass: one warp per column window; the window's 8 input rows are loaded
+// once, each tile row is summed and reduced into Y with 16-byte vector
+// reductions (the reference's fp32 atomicAdd, src/swtcf_spmm.cu:53-76 and
+// spmm_kernel.cu:2060-2093).  The SWTCF variant keeps the super-window's 32
+// repeat-cache rows in shared memory and flushes them once (src/swtcf_spmm.cu:
+// 246-264).
+#include "spmm.cuh"
+#include "primitives.cuh"
+
+#include <mutex>
+#include <vector>
+
+namespace tcc {
+
+int sm_count() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    TCC_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+    if (!cache[dev]) TCC_CUDA(cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev));
+    return cache[dev];
+}
+
+namespace {
+
+constexpr uint32_t kChunkTiles = 32;  // max tiles per warp task
+constexpr int kPullWarps = 8;         // warps per pull block
+constexpr int kPushWarps = 4;         // warps per push block
+constexpr int kStage = 136;           // floats per staged 128-feature row (bank-conflict free)
+constexpr uint32_t kOne = 0x3f800000u;
+
+struct PlanHeader {
+    uint32_t num_chunks;
+    uint32_t heavy_count;
+    uint32_t pad[14];
+};
+
+struct PlanLayout {
+    size_t cstart, desc, heavy, tmp, total;
+    uint64_t max_chunks;
+    PlanLayout(uint32_t W, uint32_t T) {
+        auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+        max_chunks = (uint64_t)W + (T + kChunkTiles - 1) / kChunkTiles + 1;
+        cstart = 256;
+        desc = cstart + al(((size_t)W + 1) * 4);
+        heavy = desc + al(max_chunks * 16);
+        tmp = heavy + al(((size_t)W + 1) * 4);
+        total = tmp + al(scan_tmp_bytes((uint64_t)W + 1));
+    }
+};
+
+__global__ void plan_count_kernel(const uint32_t* __restrict__ off, uint32_t W,
+                                  uint32_t* __restrict__ nch) {
+    const uint32_t w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w >= W) return;
+    const uint32_t t = off[w + 1] - off[w];
+    nch[w] = t <= kChunkTiles ? 1u : (t + kChunkTiles - 1) / kChunkTiles;
+}
+
+__global__ void plan_fill_kernel(const uint32_t* __restrict__ off, uint32_t W,
+                                 const uint32_t* __restrict__ cstart, uint4* __restrict__ desc,
+                                 uint32_t* __restrict__ heavy, PlanHeader* hdr) {
+    const uint32_t w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w == 0) hdr->num_chunks = cstart[W];
+    if (w >= W) return;
+    const uint32_t tb = off[w], te = off[w + 1];
+    const uint32_t base = cstart[w], n = cstart[w + 1] - cstart[w];
+    for (uint32_t j = 0; j < n; ++j) {
+        const uint32_t b = tb + j * kChunkTiles;
+        desc[base + j] = make_uint4(w, b, min(te, b + kChunkTiles), n > 1 ? 1u : 0u);
+    }
+    if (n > 1) heavy[atomicAdd(&hdr->heavy_count, 1u)] = w;
+}
+
+// Output rows of windows that several warps reduce into start from zero.
+__global__ void zero_heavy_kernel(const uint32_t* __restrict__ heavy,
+                                  const PlanHeader* __restrict__ hdr, float* __restrict__ Y,
+                                  uint64_t ldy, uint32_t F, uint32_t num_out) {
+    const uint32_t n = hdr->heavy_count;
+    for (uint32_t h = blockIdx.x; h < n; h += gridDim.x) {
+        const uint32_t w = heavy[h];
+        for (uint32_t e = threadIdx.x; e < 8 * F; e += blockDim.x) {
+            const uint32_t row = w * 8 + e / F;
+            if (row < num_out) Y[(uint64_t)row * ldy + (e % F)] = 0.f;
+        }
+    }
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+enum { kGatherDense = 0, kGatherSwtcf = 1, kGatherStore = 2 };
+
+// Row pointer of condensed column c in the hot/cold feature store
+// (cnic/src/core/spmm_kernel.cu:129-153 semantics).
+__device__ __forceinline__ const float* store_row(const FeatureStore& fs, uint32_t c, uint32_t F) {
+    const int32_t g = fs.cache_search_map[c];
+    if (g >= 0) {
+        const float* base = fs.gpu_features[g / fs.gpu_capacity];
+        return base + (uint64_t)(g % fs.gpu_capacity) * F;
+    }
+    return fs.cpu_features + (uint64_t)fs.id_map[c] * F;
+}
+
+template <int LPR, int GATHER>
+__global__ void __launch_bounds__(kPullWarps * 32) pull_kernel(PullTiles a, Dense d,
+                                                               const uint4* __restrict__ desc,
+                                                               const PlanHeader* __restrict__ hdr,
+                                                               uint32_t thr, int accumulate,
+                                                               FeatureStore fs) {
+    constexpr int G = 32 / LPR;       // column groups per warp
+    constexpr int KPG = 8 / G;        // gather columns per group
+    constexpr bool kMma = (LPR == 32);
+    __shared__ __align__(16) float stage[kMma ? kPullWarps * 8 * kStage : 4];
+
+    const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
+    const int grp = lane / LPR;
+    const int l = lane % LPR;
+    const uint32_t f = blockIdx.y * (LPR * 4) + l * 4;
+    const bool fvalid = f < d.F;
+    const uint32_t num_chunks = hdr->num_chunks;
+    const uint32_t warps_total = gridDim.x * kPullWarps;
+    float* st = stage + (kMma ? wib * 8 * kStage : 0);
+    const int gid = lane >> 2, tig = lane & 3;
+
+    for (uint32_t chunk = blockIdx.x * kPullWarps + wib; chunk < num_chunks; chunk += warps_total) {
+        const uint4 c = desc[chunk];
+        const uint32_t w = c.x;
+        float4 acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        float dacc[kMma ? 8 : 1][4];
+#pragma unroll
+        for (int j = 0; j < (kMma ? 8 : 1); ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
+        bool used_mma = false;
+        uint32_t swoff = 0;
+        if (GATHER == kGatherSwtcf) swoff = a.sw_offset[w / a.S];
+
+        for (uint32_t t = c.y; t < c.z; ++t) {
+            uint64_t bm = ld_stream_u64(a.bits + t);
+            if (a.bits_transposed) bm = transpose8x8(bm);
+            // lane k < 8 resolves gather column k of the tile
+            uint32_t my = kInvalid;
+            const float* myp = nullptr;
+            if (lane < 8) {
+                const uint32_t raw = ld_stream_u32(a.idx + (uint64_t)t * 8 + lane);
+                if constexpr (GATHER == kGatherSwtcf) {
+                    my = raw == kInvalid ? kInvalid : __ldg(a.sw_rows + swoff + raw);
+                } else {
+                    my = raw;
+                }
+                if constexpr (GATHER == kGatherStore) {
+                    if (my < a.num_in) myp = store_row(fs, my, d.F);
+                }
+            }
+            float4 x[KPG];
+#pragma unroll
+            for (int j = 0; j < KPG; ++j) {
+                const int k = grp + j * G;
+                const uint32_t ck = __shfl_sync(0xffffffffu, my, k);
+                unsigned long long pv = 0;
+                if constexpr (GATHER == kGatherStore)
+                    pv = __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(myp), k);
+                x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ck < a.num_in && fvalid) {
+                    if constexpr (GATHER == kGatherStore) {
+                        x[j] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pv) + f);
+                    } else {
+                        x[j] = ld4(d.X + (uint64_t)ck * d.ldx + f);
+                    }
+                    if (d.cs) x[j] = f4_scale(x[j], __ldg(d.cs + ck));
+                }
+            }
+            bool dense = false;
+            if constexpr (kMma) dense = (uint32_t)__popcll(bm) >= thr;
+            if (dense) {
+              if constexpr (kMma) {
+                // dense tile: D[feature][out] += X^T[feature][k] * bit(out, k)  (TF32)
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    *reinterpret_cast<float4*>(st + k * kStage + lane * 4) = x[k % KPG];
+                __syncwarp();
+                uint32_t b[2];
+                b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
+                b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t af[4];
+                    af[0] = f32_to_tf32(st[tig * kStage + 16 * j + gid]);
+                    af[1] = f32_to_tf32(st[tig * kStage + 16 * j + gid + 8]);
+                    af[2] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid]);
+                    af[3] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid + 8]);
+                    mma_tf32_16x8x8(dacc[j], af, b);
+                }
+                __syncwarp();
+                used_mma = true;
+              }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
+#pragma unroll
+                    for (int j = 0; j < KPG; ++j) {
+                        const int k = grp + j * G;
+                        if ((rb >> k) & 1u) acc[i] = f4_add(acc[i], x[j]);
+                    }
+                }
+            }
+        }
+        if constexpr (kMma) {
+          if (used_mma) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                st[(2 * tig) * kStage + 16 * j + gid] = dacc[j][0];
+                st[(2 * tig + 1) * kStage + 16 * j + gid] = dacc[j][1];
+                st[(2 * tig) * kStage + 16 * j + gid + 8] = dacc[j][2];
+                st[(2 * tig + 1) * kStage + 16 * j + gid + 8] = dacc[j][3];
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                acc[i] = f4_add(acc[i], *reinterpret_cast<const float4*>(st + i * kStage + lane * 4));
+            __syncwarp();
+          }
+        }
+        if constexpr (G > 1) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+#pragma unroll
+                for (int o = LPR; o < 32; o <<= 1) {
+                    acc[i].x += __shfl_xor_sync(0xffffffffu, acc[i].x, o);
+                    acc[i].y += __shfl_xor_sync(0xffffffffu, acc[i].y, o);
+                    acc[i].z += __shfl_xor_sync(0xffffffffu, acc[i].z, o);
+                    acc[i].w += __shfl_xor_sync(0xffffffffu, acc[i].w, o);
+                }
+            }
+        }
+        const bool heavy = c.w != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (i % G != grp) continue;
+            const uint32_t row = w * 8 + i;
+            if (row >= a.num_out || !fvalid) continue;
+            float4 v = acc[i];
+            if (d.rs) v = f4_scale(v, __ldg(d.rs + row));
+            float* yp = d.Y + (uint64_t)row * d.ldy + f;
+            if (heavy) {
+                red_add_v4(yp, v);
+            } else if (accumulate) {
+                float4 o = *reinterpret_cast<float4*>(yp);
+                *reinterpret_cast<float4*>(yp) = f4_add(o, v);
+            } else {
+                __stcs(reinterpret_cast<float4*>(yp), v);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- push ----
+template <bool SWTCF, bool STORE>
+__global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dense d, uint32_t thr,
+                                                               FeatureStore fs) {
+    __shared__ __align__(16) float stage[kPushWarps * 8 * kStage];
+    __shared__ __align__(16) float cache[SWTCF ? 32 * 128 : 4];
+    const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
+    const uint32_t f = blockIdx.y * 128 + lane * 4;
+    const bool fvalid = f < d.F;
+    float* st = stage + wib * 8 * kStage;
+    const int gid = lane >> 2, tig = lane & 3;
+
+    uint32_t w_begin, w_step, s = 0, swoff = 0;
+    uint32_t w_end = a.num_windows;
+    if (SWTCF) {
+        s = blockIdx.x;
+        w_begin = s * a.S + wib;
+        w_end = min(a.num_windows, (s + 1) * a.S);
+        w_step = kPushWarps;
+        swoff = a.sw_offset[s];
+        for (int e = threadIdx.x; e < 32 * 128; e += blockDim.x) cache[e] = 0.f;
+        __syncthreads();
+    } else {
+        w_begin = blockIdx.x * kPushWarps + wib;
+        w_step = gridDim.x * kPushWarps;
+    }
+
+    for (uint32_t w = w_begin; w < w_end; w += w_step) {
+        float4 x[8];
+        const float* xp = nullptr;
+        if (STORE && lane < 8 && w * 8 + lane < a.num_in) xp = store_row(fs, w * 8 + lane, d.F);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t cidx = w * 8 + k;
+            x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (STORE) {
+                const unsigned long long pv =
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(xp), k);
+                if (cidx < a.num_in && fvalid)
+                    x[k] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pv) + f);
+            } else if (cidx < a.num_in && fvalid) {
+                x[k] = ld4(d.X + (uint64_t)cidx * d.ldx + f);
+            }
+            if (d.cs && cidx < a.num_in) x[k] = f4_scale(x[k], __ldg(d.cs + cidx));
+        }
+        bool have_a = false;
+        uint32_t afr[8][4];
+        const uint32_t tb = a.win_offset[w], te = a.win_offset[w + 1];
+        for (uint32_t t = tb; t < te; ++t) {
+            const uint64_t bm = ld_stream_u64(a.bits + t);
+            uint32_t orow = kInvalid;
+            uint32_t cslot = 0xFFu;
+            if (lane < 8) {
+                const uint32_t raw = ld_stream_u32(a.idx + (uint64_t)t * 8 + lane);
+                if (SWTCF) {
+                    if (raw != kInvalid) {
+                        orow = __ldg(a.sw_rows + swoff + raw);
+                        cslot = __ldg(a.sw_cache_slot + swoff + raw);
+                    }
+                } else {
+                    orow = raw < a.num_out ? raw : kInvalid;
+                }
+            }
+            float4 v[8];
+            if ((uint32_t)__popcll(bm) >= thr) {
+                if (!have_a) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        *reinterpret_cast<float4*>(st + k * kStage + lane * 4) = x[k];
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        afr[j][0] = f32_to_tf32(st[tig * kStage + 16 * j + gid]);
+                        afr[j][1] = f32_to_tf32(st[tig * kStage + 16 * j + gid + 8]);
+                        afr[j][2] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid]);
+                        afr[j][3] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid + 8]);
+                    }
+                    __syncwarp();
+                    have_a = true;
+                }
+                uint32_t b[2];
+                b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
+                b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma_tf32_16x8x8(dd, afr[j], b);
+                    st[(2 * tig) * kStage + 16 * j + gid] = dd[0];
+                    st[(2 * tig + 1) * kStage + 16 * j + gid] = dd[1];
+                    st[(2 * tig) * kStage + 16 * j + gid + 8] = dd[2];
+                    st[(2 * tig + 1) * kStage + 16 * j + gid + 8] = dd[3];
+                }
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const float4*>(st + i * kStage + lane * 4);
+                __syncwarp();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
+                    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if ((rb >> k) & 1u) v[i] = f4_add(v[i], x[k]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
+                const uint32_t r = __shfl_sync(0xffffffffu, orow, i);
+                const uint32_t cs = __shfl_sync(0xffffffffu, cslot, i);
+                if (rb == 0 || r >= a.num_out || !fvalid) continue;
+                if (SWTCF && cs != 0xFFu) {
+                    float* cp = cache + cs * 128 + lane * 4;
+                    atomicAdd(cp + 0, v[i].x);
+                    atomicAdd(cp + 1, v[i].y);
+                    atomicAdd(cp + 2, v[i].z);
+                    atomicAdd(cp + 3, v[i].w);
+                } else {
+                    float4 o = v[i];
+                    if (d.rs) o = f4_scale(o, __ldg(d.rs + r));
+                    red_add_v4(d.Y + (uint64_t)r * d.ldy + f, o);
+                }
+            }
+        }
+    }
+    if (SWTCF) {
+        __syncthreads();
+        const uint32_t cc = a.sw_cached_count[s];
+        for (uint32_t c = wib; c < cc; c += kPushWarps) {
+            const uint32_t slot = a.sw_cached_row_slot[(uint64_t)s * 32 + c];
+            const uint32_t r = a.sw_rows[swoff + slot];
+            if (!fvalid || r >= a.num_out) continue;
+            float4 o = *reinterpret_cast<const float4*>(cache + c * 128 + lane * 4);
+            if (d.rs) o = f4_scale(o, __ldg(d.rs + r));
+            red_add_v4(d.Y + (uint64_t)r * d.ldy + f, o);
+        }
+    }
+}
+
+template <typename K>
+int resident_blocks(K kernel, int threads) {
+    int per_sm = 0;
+    TCC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0));
+    return std::max(1, per_sm) * sm_count();
+}
+
+template <int LPR, int GATHER>
+void launch_pull(const PullTiles& a, const Dense& d, const uint4* desc, const PlanHeader* hdr,
+                 uint64_t max_chunks, uint32_t thr, int accumulate, const FeatureStore& fs,
+                 cudaStream_t s) {
+    auto k = pull_kernel<LPR, GATHER>;
+    const uint64_t want = (max_chunks + kPullWarps - 1) / kPullWarps;
+    const unsigned gx = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(want, resident_blocks(k, kPullWarps * 32)));
+    const unsigned gy = ceil_div(d.F, LPR * 4);
+    k<<<dim3(gx, gy), kPullWarps * 32, 0, s>>>(a, d, desc, hdr, thr, accumulate, fs);
+}
+
+}  // namespace
+
+size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
+    return PlanLayout(num_windows, num_tiles).total;
+}
+
+void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int accumulate,
+               void* scratch, size_t scratch_bytes, bool plan_ready, const FeatureStore* fs,
+               cudaStream_t s) {
+    TCC_REQUIRE(d.F > 0 && d.F % 4 == 0, "F must be a positive multiple of 4");
+    TCC_REQUIRE(d.ldx % 4 == 0 && d.ldy % 4 == 0 && d.ldx >= d.F && d.ldy >= d.F,
+                "row strides must be multiples of 4 elements and >= F");
+    TCC_REQUIRE(fs || ((uintptr_t)d.X % 16 == 0), "X must be 16-byte aligned");
+    TCC_REQUIRE((uintptr_t)d.Y % 16 == 0, "Y must be 16-byte aligned");
+    if (a.num_windows == 0) return;
+    const PlanLayout L(a.num_windows, a.num_tiles);
+    TCC_REQUIRE(scratch && scratch_bytes >= L.total, "pull scratch smaller than tcc_pull_scratch_bytes()");
+    char* base = reinterpret_cast<char*>(scratch);
+    PlanHeader* hdr = reinterpret_cast<PlanHeader*>(base);
+    uint32_t* cstart = reinterpret_cast<uint32_t*>(base + L.cstart);
+    uint4* desc = reinterpret_cast<uint4*>(base + L.desc);
+    uint32_t* heavy = reinterpret_cast<uint32_t*>(base + L.heavy);
+    const uint32_t W = a.num_windows;
+    if (!plan_ready) {
+        TCC_CUDA(cudaMemsetAsync(hdr, 0, sizeof(PlanHeader), s));
+        plan_count_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart);
+        exclusive_scan<uint32_t>(cstart, cstart, W, cstart + W, base + L.tmp, s);
+        plan_fill_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart, desc, heavy, hdr);
+    }
+    if (!accumulate)
+        zero_heavy_kernel<<<std::max(1, sm_count() * 2), 256, 0, s>>>(heavy, hdr, d.Y, d.ldy, d.F,
+                                                                       a.num_out);
+    FeatureStore none;
+    const FeatureStore& f = fs ? *fs : none;
+    const bool tc = tc_threshold <= 64;
+    if (fs) {
+        launch_pull<32, kGatherStore>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+    } else if (a.sw_rows) {
+        if (tc || d.F > 64) launch_pull<32, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else if (d.F > 32) launch_pull<16, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else launch_pull<8, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+    } else {
+        if (tc || d.F > 64) launch_pull<32, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else if (d.F > 32) launch_pull<16, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else launch_pull<8, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+    }
+    TCC_CUDA(cudaGetLastError());
+}
+
+void push_spmm(const PushTiles& a, const Dense& d, uint32_t tc_threshold, const FeatureStore* fs,
+               cudaStream_t s) {
+    TCC_REQUIRE(d.F > 0 && d.F % 4 == 0, "F must be a positive multiple of 4");
+    TCC_REQUIRE(d.ldx % 4 == 0 && d.ldy % 4 == 0 && d.ldx >= d.F && d.ldy >= d.F,
+                "row strides must be multiples of 4 elements and >= F");
+    TCC_REQUIRE(fs || ((uintptr_t)d.X % 16 == 0), "X must be 16-byte aligned");
+    TCC_REQUIRE((uintptr_t)d.Y % 16 == 0, "Y must be 16-byte aligned");
+    if (a.num_windows == 0) return;
+    const unsigned gy = ceil_div(d.F, 128);
+    FeatureStore none;
+    const FeatureStore& f = fs ? *fs : none;
+    if (a.sw_rows) {
+        TCC_REQUIRE(!fs, "the SWTCF pass reads a dense X");
+        const uint32_t SW = (a.num_windows + a.S - 1) / a.S;
+        push_kernel<true, false><<<dim3(SW, gy), kPushWarps * 32, 0, s>>>(a, d, tc_threshold, f);
+    } else {
+        const unsigned want = ceil_div(a.num_windows, kPushWarps);
+        if (fs) {
+            auto k = push_kernel<false, true>;
+            const unsigned gx = std::max(1u, std::min<unsigned>(want, resident_blocks(k, kPushWarps * 32)));
+            k<<<dim3(gx, gy), kPushWarps * 32, 0, s>>>(a, d, tc_threshold, f);
+        } else {
+            auto k = push_kernel<false, false>;
+            const unsigned gx = std::max(1u, std::min<unsigned>(want, resident_blocks(k, kPushWarps * 32)));
+            k<<<dim3(gx, gy), kPushWarps * 32, 0, s>>>(a, d, tc_threshold, f);
+        }
+    }
+    TCC_CUDA(cudaGetLastError());
+}
+
+}  // namespace tcc

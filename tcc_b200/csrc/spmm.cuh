@@ -1,0 +1,70 @@
+// spmm.cuh -- SpMM over 8x8 window tiles (internal interface used by capi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace tcc {
+
+// Tile source of a pull pass (owner-computes: window w owns outputs 8w..8w+7).
+struct PullTiles {
+    uint32_t num_windows;
+    uint32_t num_tiles;
+    const uint32_t* win_offset;  // [num_windows+1]
+    const uint64_t* bits;        // [num_tiles]
+    const uint32_t* idx;         // [8*num_tiles]: gather index, or SWTCF row slot
+    bool bits_transposed;        // false: bit = out*8 + gather (BCSR); true: gather*8 + out
+    // SWTCF transposed pass: gather row = sw_rows[sw_offset[w / S] + slot]
+    const uint32_t* sw_offset = nullptr;
+    const uint32_t* sw_rows = nullptr;
+    uint32_t S = 0;
+    uint32_t num_out;   // output rows (guards the last window)
+    uint32_t num_in;    // gather rows (indices >= num_in are padding)
+};
+
+// Dense operands.  cs scales gathered rows, rs scales output rows (NULL = 1).
+struct Dense {
+    const float* X;
+    uint64_t ldx;
+    float* Y;
+    uint64_t ldy;
+    uint32_t F;
+    const float* rs;
+    const float* cs;
+};
+
+// Hot/cold feature store of the mixed first-layer pass.
+struct FeatureStore {
+    const int32_t* id_map = nullptr;
+    const float* cpu_features = nullptr;
+    const int32_t* cache_search_map = nullptr;
+    const float* const* gpu_features = nullptr;
+    int64_t gpu_capacity = 0;
+};
+
+size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
+void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int accumulate,
+               void* scratch, size_t scratch_bytes, bool plan_ready, const FeatureStore* fs,
+               cudaStream_t s);
+
+// Tile source of a push pass (window w owns inputs 8w..8w+7 and scatters).
+struct PushTiles {
+    uint32_t num_windows;
+    const uint32_t* win_offset;
+    const uint64_t* bits;       // bit = outslot*8 + local input
+    const uint32_t* idx;        // BCSC: output row; SWTCF: super-window row slot
+    // SWTCF: output row = sw_rows[sw_offset[s] + slot]; repeat cache per super-window
+    const uint32_t* sw_offset = nullptr;
+    const uint32_t* sw_rows = nullptr;
+    const uint8_t* sw_cache_slot = nullptr;
+    const uint32_t* sw_cached_row_slot = nullptr;
+    const uint8_t* sw_cached_count = nullptr;
+    uint32_t S = 0;
+    uint32_t num_out;
+    uint32_t num_in;
+};
+
+// Y += diag(rs) * A * diag(cs) * X over column windows (vector fp32 reductions).
+void push_spmm(const PushTiles& a, const Dense& d, uint32_t tc_threshold, const FeatureStore* fs,
+               cudaStream_t s);
+
+}  // namespace tcc

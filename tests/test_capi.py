@@ -1,0 +1,62 @@
+"""The C-ABI library: loads, exports every symbol include/tcc_b200.h declares,
+and rejects bad arguments before touching a GPU (CPU only)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    text = open(os.path.join(ROOT, "include", "tcc_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tcc_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from tcc_b200 import build, _lib
+    build.build()
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from tcc_b200 import _lib
+    names = declared_symbols()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.PROTOTYPES, f"{n} has no ctypes prototype"
+
+
+def test_version_and_scratch_query(lib):
+    assert b"sm_100a" in lib.tcc_version()
+    assert lib.tcc_pull_scratch_bytes(1000, 5000) > 0
+    assert lib.tcc_pull_scratch_bytes(2000, 5000) > lib.tcc_pull_scratch_bytes(1000, 5000)
+
+
+def test_null_arguments_are_rejected_without_a_gpu(lib):
+    from tcc_b200 import _lib
+    assert lib.tcc_swtcf_alloc(None, 4, 4, 4, 16) == 1
+    assert b"null" in lib.tcc_last_error()
+    m = _lib.Swtcf()
+    assert lib.tcc_swtcf_alloc(C.byref(m), 4, 0, 4, 16) == 1          # cols == 0
+    assert lib.tcc_swtcf_alloc(C.byref(m), 4, 4, 4, 33) == 1          # S > 32
+    assert lib.tcc_swtcf_spmm(None, None, None, 12, None) == 1
+    assert lib.tcc_bcsr_spmm(None, None, 0, None, 0, 128, 12, None, None, 0, None, 0, 0, None) == 1
+    ws = C.c_void_p()
+    assert lib.tcc_swtcf_workspace_create(C.byref(ws), 0, 10, 16) == 1
+    assert lib.tcc_tiles_workspace_create(C.byref(ws), 10, 0, 10) == 1
+    with pytest.raises(_lib.TccError):
+        _lib.call("tcc_swtcf_spmm", None, None, None, 12, None)
+
+
+def test_reference_build_exports_harness():
+    path = os.path.join(ROOT, "oracle", "_ref", "libtcc_ref.so")
+    if not os.path.exists(path):
+        pytest.skip("reference build absent (built by `make -C oracle ref`)")
+    L = C.CDLL(path)
+    for n in ("ref_swtcf_convert", "ref_swtcf_spmm", "ref_cnic_spmm"):
+        assert hasattr(L, n)
