@@ -60,10 +60,18 @@ __device__ __forceinline__ uint32_t f32_to_tf32(float x) {
     return r;
 }
 
+// Round-to-nearest (ties away from zero) to TF32 on the integer pipes: add
+// half a TF32 ulp to the magnitude bits and clear the 13 dropped bits.  Same
+// result as the documented cvt.rna mode for finite inputs, without the
+// conversion-unit round trip.
+__device__ __forceinline__ uint32_t tf32_rna_bits(float x) {
+    return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
+}
+
 // D[16x8] += A[16x8] * B[8x8], TF32 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma_tf32_16x8x8(float d[4], const uint32_t a[4],
                                                 const uint32_t b[2]) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

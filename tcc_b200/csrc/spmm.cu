@@ -38,8 +38,7 @@ int sm_count() {
 
 namespace {
 
-constexpr uint32_t kChunkTiles = 32;  // max tiles per warp task
-constexpr int kPullWarps = 8;         // warps per pull block
+constexpr uint32_t kChunkTiles = 16;  // max tiles per warp task
 constexpr int kPushWarps = 4;         // warps per push block
 constexpr int kStage = 136;           // floats per staged 128-feature row (bank-conflict free)
 constexpr uint32_t kOne = 0x3f800000u;
@@ -118,159 +117,226 @@ __device__ __forceinline__ const float* store_row(const FeatureStore& fs, uint32
     return fs.cpu_features + (uint64_t)fs.id_map[c] * F;
 }
 
-template <int LPR, int GATHER>
-__global__ void __launch_bounds__(kPullWarps * 32) pull_kernel(PullTiles a, Dense d,
-                                                               const uint4* __restrict__ desc,
-                                                               const PlanHeader* __restrict__ hdr,
-                                                               uint32_t thr, int accumulate,
-                                                               FeatureStore fs) {
-    constexpr int G = 32 / LPR;       // column groups per warp
-    constexpr int KPG = 8 / G;        // gather columns per group
-    constexpr bool kMma = (LPR == 32);
-    __shared__ __align__(16) float stage[kMma ? kPullWarps * 8 * kStage : 4];
+__device__ __forceinline__ float comp(const float4& v, int c) {
+    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+}
 
-    const int lane = threadIdx.x & 31;
-    const int wib = threadIdx.x >> 5;
-    const int grp = lane / LPR;
-    const int l = lane % LPR;
-    const uint32_t f = blockIdx.y * (LPR * 4) + l * 4;
-    const bool fvalid = f < d.F;
-    const uint32_t num_chunks = hdr->num_chunks;
-    const uint32_t warps_total = gridDim.x * kPullWarps;
-    float* st = stage + (kMma ? wib * 8 * kStage : 0);
-    const int gid = lane >> 2, tig = lane & 3;
+// Tile MMAs of one 8x8 tile.  The warp's 64*NP features are permuted across
+// MMA slots so that each lane's float4 gathers feed the A fragments directly:
+// MMA j = 4p + c, slot m holds feature 4*(m + 16p) + c.  Lane (gid, tig) holds
+// x[r][s] = X[gather row k = tig + 4r][4*(gid + 8s) .. +3]; B[k][n] = bit(n*8+k).
+// pass2 == false: one TF32 pass with operands rounded like cvt.rna (the
+// reference's dense-tile arithmetic).  pass2 == true: fp32-accurate split
+// x = hi + lo (hi = x with the low 13 bits cleared, exact), all hi MMAs
+// first, then all lo MMAs.
+template <int NP>
+__device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 (&x)[2][2 * NP],
+                                         uint64_t bm, int gid, int tig, bool pass2) {
+    uint32_t b[2];
+    b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
+    b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
+    if (!pass2) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t a[4] = {tf32_rna_bits(comp(x[0][2 * p], c)), tf32_rna_bits(comp(x[0][2 * p + 1], c)),
+                                       tf32_rna_bits(comp(x[1][2 * p], c)), tf32_rna_bits(comp(x[1][2 * p + 1], c))};
+                mma_tf32_16x8x8(dacc[4 * p + c], a, b);
+            }
+        return;
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t hi[4] = {
+                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
+            mma_tf32_16x8x8(dacc[4 * p + c], hi, b);
+        }
+    // lo = x - hi is exact in fp32; recomputed here to keep registers free
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float v[4] = {comp(x[0][2 * p], c), comp(x[0][2 * p + 1], c),
+                                comp(x[1][2 * p], c), comp(x[1][2 * p + 1], c)};
+            uint32_t lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                lo[e] = __float_as_uint(v[e] - __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
+            mma_tf32_16x8x8(dacc[4 * p + c], lo, b);
+        }
+}
 
-    for (uint32_t chunk = blockIdx.x * kPullWarps + wib; chunk < num_chunks; chunk += warps_total) {
-        const uint4 c = desc[chunk];
-        const uint32_t w = c.x;
-        float4 acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        float dacc[kMma ? 8 : 1][4];
-#pragma unroll
-        for (int j = 0; j < (kMma ? 8 : 1); ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
-        bool used_mma = false;
-        uint32_t swoff = 0;
-        if (GATHER == kGatherSwtcf) swoff = a.sw_offset[w / a.S];
+// ---------------------------------------------------------------- pull ----
+// One warp per chunk; the 8 gather rows of a tile go straight to registers
+// as 128-bit L1::no_allocate loads in MMA fragment order, two tiles in flight
+// per warp, 16 warps/SM.  Chunk metadata (bitmaps, gather indices) is
+// double-buffered in shared memory with cp.async one chunk ahead.
+constexpr int kPullWarps = 8;
+struct WarpMeta {
+    uint64_t bits[kChunkTiles];
+    uint32_t idx[kChunkTiles * 8];
+};
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
-        for (uint32_t t = c.y; t < c.z; ++t) {
-            uint64_t bm = ld_stream_u64(a.bits + t);
-            if (a.bits_transposed) bm = transpose8x8(bm);
-            // lane k < 8 resolves gather column k of the tile
-            uint32_t my = kInvalid;
-            const float* myp = nullptr;
-            if (lane < 8) {
-                const uint32_t raw = ld_stream_u32(a.idx + (uint64_t)t * 8 + lane);
-                if constexpr (GATHER == kGatherSwtcf) {
-                    my = raw == kInvalid ? kInvalid : __ldg(a.sw_rows + swoff + raw);
-                } else {
-                    my = raw;
-                }
-                if constexpr (GATHER == kGatherStore) {
-                    if (my < a.num_in) myp = store_row(fs, my, d.F);
-                }
-            }
-            float4 x[KPG];
+template <int NP, int GATHER>
+__device__ __forceinline__ void gather_tile(float4 (&x)[2][2 * NP], const PullTiles& a,
+                                            const Dense& d, const WarpMeta& M,
+                                            const float* const* ptrs, int t, int gid, int tig,
+                                            uint32_t fb) {
 #pragma unroll
-            for (int j = 0; j < KPG; ++j) {
-                const int k = grp + j * G;
-                const uint32_t ck = __shfl_sync(0xffffffffu, my, k);
-                unsigned long long pv = 0;
-                if constexpr (GATHER == kGatherStore)
-                    pv = __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(myp), k);
-                x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (ck < a.num_in && fvalid) {
-                    if constexpr (GATHER == kGatherStore) {
-                        x[j] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pv) + f);
-                    } else {
-                        x[j] = ld4(d.X + (uint64_t)ck * d.ldx + f);
-                    }
-                    if (d.cs) x[j] = f4_scale(x[j], __ldg(d.cs + ck));
-                }
-            }
-            bool dense = false;
-            if constexpr (kMma) dense = (uint32_t)__popcll(bm) >= thr;
-            if (dense) {
-              if constexpr (kMma) {
-                // dense tile: D[feature][out] += X^T[feature][k] * bit(out, k)  (TF32)
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    *reinterpret_cast<float4*>(st + k * kStage + lane * 4) = x[k % KPG];
-                __syncwarp();
-                uint32_t b[2];
-                b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
-                b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    uint32_t af[4];
-                    af[0] = f32_to_tf32(st[tig * kStage + 16 * j + gid]);
-                    af[1] = f32_to_tf32(st[tig * kStage + 16 * j + gid + 8]);
-                    af[2] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid]);
-                    af[3] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid + 8]);
-                    mma_tf32_16x8x8(dacc[j], af, b);
-                }
-                __syncwarp();
-                used_mma = true;
-              }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
-#pragma unroll
-                    for (int j = 0; j < KPG; ++j) {
-                        const int k = grp + j * G;
-                        if ((rb >> k) & 1u) acc[i] = f4_add(acc[i], x[j]);
-                    }
-                }
-            }
+    for (int r = 0; r < 2; ++r) {
+        const uint32_t k = M.idx[t * 8 + tig + 4 * r];
+        const bool ok = k < a.num_in;
+        const float* row = nullptr;
+        if constexpr (GATHER == kGatherStore) {
+            row = ok ? ptrs[t * 8 + tig + 4 * r] : nullptr;
+        } else {
+            row = d.X + (uint64_t)(ok ? k : 0) * d.ldx;
         }
-        if constexpr (kMma) {
-          if (used_mma) {
+        const float sc = (ok && d.cs) ? __ldg(d.cs + k) : 1.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                st[(2 * tig) * kStage + 16 * j + gid] = dacc[j][0];
-                st[(2 * tig + 1) * kStage + 16 * j + gid] = dacc[j][1];
-                st[(2 * tig) * kStage + 16 * j + gid + 8] = dacc[j][2];
-                st[(2 * tig + 1) * kStage + 16 * j + gid + 8] = dacc[j][3];
+        for (int s = 0; s < 2 * NP; ++s) {
+            const uint32_t f = fb + 4 * (gid + 8 * s);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ok && f < d.F) {
+                if constexpr (GATHER == kGatherStore) v = *reinterpret_cast<const float4*>(row + f);
+                else v = ld4(row + f);
             }
-            __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                acc[i] = f4_add(acc[i], *reinterpret_cast<const float4*>(st + i * kStage + lane * 4));
-            __syncwarp();
-          }
-        }
-        if constexpr (G > 1) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-#pragma unroll
-                for (int o = LPR; o < 32; o <<= 1) {
-                    acc[i].x += __shfl_xor_sync(0xffffffffu, acc[i].x, o);
-                    acc[i].y += __shfl_xor_sync(0xffffffffu, acc[i].y, o);
-                    acc[i].z += __shfl_xor_sync(0xffffffffu, acc[i].z, o);
-                    acc[i].w += __shfl_xor_sync(0xffffffffu, acc[i].w, o);
-                }
-            }
-        }
-        const bool heavy = c.w != 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (i % G != grp) continue;
-            const uint32_t row = w * 8 + i;
-            if (row >= a.num_out || !fvalid) continue;
-            float4 v = acc[i];
-            if (d.rs) v = f4_scale(v, __ldg(d.rs + row));
-            float* yp = d.Y + (uint64_t)row * d.ldy + f;
-            if (heavy) {
-                red_add_v4(yp, v);
-            } else if (accumulate) {
-                float4 o = *reinterpret_cast<float4*>(yp);
-                *reinterpret_cast<float4*>(yp) = f4_add(o, v);
-            } else {
-                __stcs(reinterpret_cast<float4*>(yp), v);
-            }
+            x[r][s] = f4_scale(v, sc);
         }
     }
+}
+
+template <int NP, int GATHER>
+__global__ void __launch_bounds__(kPullWarps * 32, 2) pull_kernel(PullTiles a, Dense d,
+                                                                  const uint4* __restrict__ desc,
+                                                                  PlanHeader* __restrict__ hdr,
+                                                                  uint32_t thr, int accumulate,
+                                                                  FeatureStore fs) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    WarpMeta* meta = reinterpret_cast<WarpMeta*>(smem_raw) + 2 * wib;
+    const float** ptrs = nullptr;
+    if constexpr (GATHER == kGatherStore)
+        ptrs = reinterpret_cast<const float**>(smem_raw + sizeof(WarpMeta) * 2 * kPullWarps) +
+               wib * kChunkTiles * 8;
+    const uint32_t fb = blockIdx.y * (64 * NP);
+    const uint32_t num_chunks = hdr->num_chunks;
+    const uint32_t warps_total = gridDim.x * kPullWarps;
+
+    auto prefetch = [&](const uint4& c, int b) {
+        const uint32_t n = c.z - c.y;
+        if ((uint32_t)lane < n) cp_async8(&meta[b].bits[lane], a.bits + c.y + lane);
+        for (uint32_t p = lane; p < 2 * n; p += 32)
+            cp_async16(&meta[b].idx[p * 4], a.idx + (uint64_t)c.y * 8 + p * 4);
+    };
+
+    uint32_t chunk = blockIdx.x * kPullWarps + wib;
+    uint4 cur = make_uint4(0, 0, 0, 0), nxt = make_uint4(0, 0, 0, 0);
+    if (chunk < num_chunks) {
+        cur = desc[chunk];
+        prefetch(cur, 0);
+    }
+    cp_async_commit();
+    if (chunk + warps_total < num_chunks) nxt = desc[chunk + warps_total];
+    int buf = 0;
+    while (chunk < num_chunks) {
+        const uint32_t next = chunk + warps_total;
+        if (next < num_chunks) prefetch(nxt, buf ^ 1);
+        cp_async_commit();
+        uint4 nxt2 = make_uint4(0, 0, 0, 0);
+        if (next + warps_total < num_chunks) nxt2 = desc[next + warps_total];
+        cp_async_wait<1>();
+        __syncwarp();
+        WarpMeta& M = meta[buf];
+        const uint32_t w = cur.x;
+        const int n = (int)(cur.z - cur.y);
+        if constexpr (GATHER == kGatherSwtcf) {
+            const uint32_t swoff = a.sw_offset[w / a.S];
+            for (int e = lane; e < n * 8; e += 32) {
+                const uint32_t slot = M.idx[e];
+                M.idx[e] = slot == kInvalid ? kInvalid : __ldg(a.sw_rows + swoff + slot);
+            }
+            __syncwarp();
+        }
+        if constexpr (GATHER == kGatherStore) {
+            for (int e = lane; e < n * 8; e += 32) {
+                const uint32_t c = M.idx[e];
+                ptrs[e] = c < a.num_in ? store_row(fs, c, d.F) : nullptr;
+            }
+            __syncwarp();
+        }
+        float dacc[4 * NP][4];
+#pragma unroll
+        for (int j = 0; j < 4 * NP; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
+        for (int t = 0; t < n; t += 2) {
+            float4 xa[2][2 * NP], xb[2][2 * NP];
+            gather_tile<NP, GATHER>(xa, a, d, M, ptrs, t, gid, tig, fb);
+            const bool two = t + 1 < n;
+            if (two) gather_tile<NP, GATHER>(xb, a, d, M, ptrs, t + 1, gid, tig, fb);
+            uint64_t bma = M.bits[t];
+            if (a.bits_transposed) bma = transpose8x8(bma);
+            tile_mma<NP>(dacc, xa, bma, gid, tig, (uint32_t)__popcll(bma) < thr);
+            if (two) {
+                uint64_t bmb = M.bits[t + 1];
+                if (a.bits_transposed) bmb = transpose8x8(bmb);
+                tile_mma<NP>(dacc, xb, bmb, gid, tig, (uint32_t)__popcll(bmb) < thr);
+            }
+        }
+        // epilogue: lane holds output rows 2tig, 2tig+1 at float4 slots q = gid + 8s
+        const bool heavy = cur.w != 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t row = w * 8 + 2 * tig + h;
+            if (row >= a.num_out) continue;
+            const float rsc = d.rs ? __ldg(d.rs + row) : 1.f;
+            float* yrow = d.Y + (uint64_t)row * d.ldy;
+#pragma unroll
+            for (int s = 0; s < 2 * NP; ++s) {
+                const uint32_t f = fb + 4 * (gid + 8 * s);
+                if (f >= d.F) continue;
+                const int p = s >> 1, e = (s & 1) * 2 + h;  // d[.][e]: rows (2tig | 2tig+1), m (gid | gid+8)
+                float4 v = make_float4(dacc[4 * p + 0][e], dacc[4 * p + 1][e], dacc[4 * p + 2][e],
+                                       dacc[4 * p + 3][e]);
+                v = f4_scale(v, rsc);
+                float* yp = yrow + f;
+                if (heavy) {
+                    red_add_v4(yp, v);
+                } else if (accumulate) {
+                    const float4 o = *reinterpret_cast<float4*>(yp);
+                    *reinterpret_cast<float4*>(yp) = f4_add(o, v);
+                } else {
+                    __stcs(reinterpret_cast<float4*>(yp), v);
+                }
+            }
+        }
+        __syncwarp();
+        buf ^= 1;
+        chunk = next;
+        cur = nxt;
+        nxt = nxt2;
+    }
+    cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------- push ----
@@ -421,15 +487,21 @@ int resident_blocks(K kernel, int threads) {
     return std::max(1, per_sm) * sm_count();
 }
 
-template <int LPR, int GATHER>
-void launch_pull(const PullTiles& a, const Dense& d, const uint4* desc, const PlanHeader* hdr,
-                 uint64_t max_chunks, uint32_t thr, int accumulate, const FeatureStore& fs,
-                 cudaStream_t s) {
-    auto k = pull_kernel<LPR, GATHER>;
+template <int NP, int GATHER>
+void launch_pull(const PullTiles& a, const Dense& d, const uint4* desc, PlanHeader* hdr,
+                     uint64_t max_chunks, uint32_t thr, int accumulate, const FeatureStore& fs,
+                     cudaStream_t s) {
+    auto k = pull_kernel<NP, GATHER>;
+    size_t smem = sizeof(WarpMeta) * 2 * kPullWarps;
+    if (GATHER == kGatherStore) smem += sizeof(void*) * kChunkTiles * 8 * kPullWarps;
+    TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    TCC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kPullWarps * 32, smem));
     const uint64_t want = (max_chunks + kPullWarps - 1) / kPullWarps;
-    const unsigned gx = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(want, resident_blocks(k, kPullWarps * 32)));
-    const unsigned gy = ceil_div(d.F, LPR * 4);
-    k<<<dim3(gx, gy), kPullWarps * 32, 0, s>>>(a, d, desc, hdr, thr, accumulate, fs);
+    const uint64_t resident = (uint64_t)std::max(1, per_sm) * sm_count();
+    const unsigned gx = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(want, resident));
+    const unsigned gy = ceil_div(d.F, 64 * NP);
+    k<<<dim3(gx, gy), kPullWarps * 32, smem, s>>>(a, d, desc, hdr, thr, accumulate, fs);
 }
 
 }  // namespace
@@ -446,6 +518,8 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
                 "row strides must be multiples of 4 elements and >= F");
     TCC_REQUIRE(fs || ((uintptr_t)d.X % 16 == 0), "X must be 16-byte aligned");
     TCC_REQUIRE((uintptr_t)d.Y % 16 == 0, "Y must be 16-byte aligned");
+    TCC_REQUIRE((uintptr_t)a.idx % 16 == 0 && (uintptr_t)a.bits % 8 == 0,
+                "tile index / bitmap arrays must be 16 / 8-byte aligned");
     if (a.num_windows == 0) return;
     const PlanLayout L(a.num_windows, a.num_tiles);
     TCC_REQUIRE(scratch && scratch_bytes >= L.total, "pull scratch smaller than tcc_pull_scratch_bytes()");
@@ -466,17 +540,17 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
                                                                        a.num_out);
     FeatureStore none;
     const FeatureStore& f = fs ? *fs : none;
-    const bool tc = tc_threshold <= 64;
+    // 64 features per MMA pass pair: F <= 64 uses one, wider F two per block
+    const bool narrow = d.F <= 64;
     if (fs) {
-        launch_pull<32, kGatherStore>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        if (narrow) launch_pull<1, kGatherStore>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else launch_pull<2, kGatherStore>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
     } else if (a.sw_rows) {
-        if (tc || d.F > 64) launch_pull<32, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
-        else if (d.F > 32) launch_pull<16, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
-        else launch_pull<8, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        if (narrow) launch_pull<1, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else launch_pull<2, kGatherSwtcf>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
     } else {
-        if (tc || d.F > 64) launch_pull<32, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
-        else if (d.F > 32) launch_pull<16, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
-        else launch_pull<8, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        if (narrow) launch_pull<1, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
+        else launch_pull<2, kGatherDense>(a, d, desc, hdr, L.max_chunks, tc_threshold, accumulate, f, s);
     }
     TCC_CUDA(cudaGetLastError());
 }
