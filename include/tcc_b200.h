@@ -185,6 +185,24 @@ tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float*
                          uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
                          const float* cs, int accumulate, void* scratch, size_t scratch_bytes,
                          int plan_ready, cudaStream_t stream);
+/* No counterpart in the reference.  tcc_bcsr_spmm for callers that cannot
+ * allocate device memory -- code that runs where cudaMalloc is not allowed
+ * (inside a host-side memory pool's or allocator's own callbacks, plug-ins of
+ * hosts that own all device memory, pre-planned real-time loops that forbid
+ * allocation after start-up).  Same arguments and result as tcc_bcsr_spmm with
+ * accumulate/scales, but the work plan lives in a scratch array built into
+ * this library (TCC_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads
+ * the library until exit) instead of caller scratch; nothing is allocated.
+ *  - Tilings whose plan exceeds TCC_NOALLOC_SCRATCH_BYTES are rejected with
+ *    TCC_ERR_CAPACITY (about 24 bytes per window plus 1 per tile).
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - Every call rebuilds the plan in the same array: calls that overlap on the
+ *    GPU (other streams, other host threads) race and must be serialised. */
+#define TCC_NOALLOC_SCRATCH_BYTES (16u << 20)
+tcc_status tcc_bcsr_spmm_noalloc(const tcc_bcsr* a, const float* B, uint64_t ldb, float* C,
+                                 uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
+                                 const float* cs, int accumulate, cudaStream_t stream);
 /* tf32_spmm_bcsc + tf32_computeX128TransposePipe2_BCSC
  * (cnic/src/core/spmm_dispatcher.cu:235-302, spmm_kernel.cu:1844-2167): the
  * column-window push pass, C += diag(rs) * A * diag(cs) * B, accumulated with

@@ -15,6 +15,7 @@ TCC_OK = 0
 STATUS_NAMES = {0: "TCC_OK", 1: "TCC_ERR_INVALID_ARGUMENT", 2: "TCC_ERR_CUDA",
                 3: "TCC_ERR_OUT_OF_MEMORY", 4: "TCC_ERR_UNSUPPORTED", 5: "TCC_ERR_DEVICE",
                 6: "TCC_ERR_CAPACITY"}
+NOALLOC_SCRATCH_BYTES = 16 << 20  # TCC_NOALLOC_SCRATCH_BYTES
 TILES_BCSR = 0
 TILES_BCSC = 1
 DEVERR_GROUP_DEGREE = 1
@@ -88,6 +89,8 @@ PROTOTYPES = {
     "tcc_pull_scratch_bytes": (C.c_size_t, [_u32, _u32]),
     "tcc_bcsr_spmm": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i, _vp,
                             C.c_size_t, _i, _vp]),
+    "tcc_bcsr_spmm_noalloc": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
+                                    _i, _vp]),
     "tcc_bcsc_spmm": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),
     "tcc_bcsc_spmm_t": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i,
                               _vp, C.c_size_t, _i, _vp]),

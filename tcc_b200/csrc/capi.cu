@@ -4,6 +4,7 @@
 #include "convert.cuh"
 #include "spmm.cuh"
 
+#include <mutex>
 #include <string>
 
 struct tcc_swtcf_workspace {
@@ -82,6 +83,31 @@ tcc::PushTiles bcsc_push(const tcc_bcsc* a) {
     t.num_out = a->num_rows;
     t.num_in = a->num_cols;
     return t;
+}
+
+// Scratch of tcc_bcsr_spmm_noalloc: a fixed device array in this library's
+// image (every GPU that loads the library holds it until exit), so the entry
+// point never allocates.  Host code reaches it only through the address that
+// cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[TCC_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (the first call on a device does this set-up).
+void* noalloc_scratch() {
+    int dev = 0;
+    TCC_CUDA(cudaGetDevice(&dev));
+    TCC_REQUIRE(dev >= 0 && dev < kMaxDevices, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        TCC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_ptr[dev] = p;
+    }
+    return g_noalloc_ptr[dev];
 }
 
 void check_bcsr(const tcc_bcsr* a) {
@@ -349,6 +375,27 @@ tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float*
         tcc::Dense d{B, ldb, C, ldc, F, rs, cs};
         tcc::pull_spmm(bcsr_pull(a), d, tc_threshold, accumulate, scratch, scratch_bytes,
                        plan_ready != 0, nullptr, stream);
+    });
+}
+
+tcc_status tcc_bcsr_spmm_noalloc(const tcc_bcsr* a, const float* B, uint64_t ldb, float* C,
+                                 uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
+                                 const float* cs, int accumulate, cudaStream_t stream) {
+    return guarded("tcc_bcsr_spmm_noalloc", [&] {
+        check_bcsr(a);
+        TCC_REQUIRE(B && C, "null argument");
+        const size_t need = tcc::pull_scratch_bytes(a->num_rowWindows, a->num_TCBlocks);
+        if (need > TCC_NOALLOC_SCRATCH_BYTES)
+            throw tcc::Error(TCC_ERR_CAPACITY,
+                             "tiling needs " + std::to_string(need) +
+                                 " bytes of plan scratch; the built-in scratch holds " +
+                                 std::to_string((size_t)TCC_NOALLOC_SCRATCH_BYTES) +
+                                 " (use tcc_bcsr_spmm with caller scratch)");
+        // the shared array keeps the last call's plan: always rebuild it (the
+        // rebuild clears the plan header that must start at zero)
+        tcc::Dense d{B, ldb, C, ldc, F, rs, cs};
+        tcc::pull_spmm(bcsr_pull(a), d, tc_threshold, accumulate, noalloc_scratch(),
+                       TCC_NOALLOC_SCRATCH_BYTES, false, nullptr, stream);
     });
 }
 

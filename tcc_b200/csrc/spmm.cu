@@ -21,17 +21,16 @@
 #include "primitives.cuh"
 
 #include <mutex>
-#include <vector>
 
 namespace tcc {
 
 int sm_count() {
     static std::mutex mu;
-    static std::vector<int> cache;
+    static int cache[64] = {};
     int dev = 0;
     TCC_CUDA(cudaGetDevice(&dev));
+    TCC_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
     std::lock_guard<std::mutex> lock(mu);
-    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
     if (!cache[dev]) TCC_CUDA(cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev));
     return cache[dev];
 }
