@@ -210,6 +210,14 @@ tcc_status tcc_bcsr_spmm_noalloc(const tcc_bcsr* a, const float* B, uint64_t ldb
 tcc_status tcc_bcsc_spmm(const tcc_bcsc* a, const float* B, uint64_t ldb, float* C,
                          uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
                          const float* cs, cudaStream_t stream);
+/* The transposed pass over BCSR tiles, as a push: Z[num_cols x F] +=
+ * diag(cs) * A^T * diag(rs) * G[num_rows x F] with vector fp32 reductions.  The
+ * backward of the BCSR part of a split (BCSR + BCSC) matrix; replaces
+ * torch.sparse.mm(A_topo.T, d_output) of train/tcgnn_conv_release.py:150-154 for
+ * that part. */
+tcc_status tcc_bcsr_spmm_t(const tcc_bcsr* a, const float* G, uint64_t ldg, float* Z,
+                           uint64_t ldz, uint32_t F, uint32_t tc_threshold, const float* rs,
+                           const float* cs, cudaStream_t stream);
 /* The transposed (backward) pass over BCSC tiles: Z[num_cols x F] =
  * diag(cs) * A^T * diag(rs) * G[num_rows x F], owner-computes per column
  * window.  Replaces torch.sparse.mm(A_topo.T, d_output) of

@@ -91,6 +91,7 @@ PROTOTYPES = {
                             C.c_size_t, _i, _vp]),
     "tcc_bcsr_spmm_noalloc": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
                                     _i, _vp]),
+    "tcc_bcsr_spmm_t": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),
     "tcc_bcsc_spmm": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),
     "tcc_bcsc_spmm_t": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i,
                               _vp, C.c_size_t, _i, _vp]),

@@ -110,6 +110,20 @@ void* noalloc_scratch() {
     return g_noalloc_ptr[dev];
 }
 
+// Transposed pass over BCSR tiles as a push: window w scatters rows 8w..8w+7
+// of G into rows sparseA2B[.] of Z (bit = inrow*8 + k, transposed on load).
+tcc::PushTiles bcsr_push_t(const tcc_bcsr* a) {
+    tcc::PushTiles t{};
+    t.num_windows = a->num_rowWindows;
+    t.win_offset = a->rowWindowOffset;
+    t.bits = a->tcLocalBit;
+    t.idx = a->sparseA2B;
+    t.bits_transposed = true;
+    t.num_out = a->num_cols;
+    t.num_in = a->num_rows;
+    return t;
+}
+
 void check_bcsr(const tcc_bcsr* a) {
     TCC_REQUIRE(a && a->rowWindowOffset && a->tcLocalBit && a->sparseA2B, "BCSR arrays missing");
     TCC_REQUIRE(a->num_rowWindows == (a->num_rows + 7) / 8, "num_rowWindows != ceil(num_rows/8)");
@@ -396,6 +410,18 @@ tcc_status tcc_bcsr_spmm_noalloc(const tcc_bcsr* a, const float* B, uint64_t ldb
         tcc::Dense d{B, ldb, C, ldc, F, rs, cs};
         tcc::pull_spmm(bcsr_pull(a), d, tc_threshold, accumulate, noalloc_scratch(),
                        TCC_NOALLOC_SCRATCH_BYTES, false, nullptr, stream);
+    });
+}
+
+tcc_status tcc_bcsr_spmm_t(const tcc_bcsr* a, const float* G, uint64_t ldg, float* Z, uint64_t ldz,
+                           uint32_t F, uint32_t tc_threshold, const float* rs, const float* cs,
+                           cudaStream_t stream) {
+    return guarded("tcc_bcsr_spmm_t", [&] {
+        check_bcsr(a);
+        TCC_REQUIRE(G && Z, "null argument");
+        // Z += diag(cs) A^T diag(rs) G: G rows (window inputs) scaled by rs, Z rows by cs
+        tcc::Dense d{G, ldg, Z, ldz, F, cs, rs};
+        tcc::push_spmm(bcsr_push_t(a), d, tc_threshold, nullptr, stream);
     });
 }
 

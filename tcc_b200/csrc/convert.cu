@@ -94,24 +94,40 @@ __global__ void groups_kernel(const uint64_t* __restrict__ keys, const uint32_t*
 }
 
 // ---------------------------------------------------------------- step 4 --
-__global__ void window_count_kernel(const uint64_t* __restrict__ gkey,
-                                    const uint32_t* __restrict__ gmask,
-                                    const uint32_t* __restrict__ gstart,
-                                    const uint32_t* __restrict__ d_ng, uint64_t n, int ybits,
-                                    uint32_t W, uint32_t* __restrict__ wcnt, uint32_t* err) {
+// Duplicate check per group: a group's edge count must equal its popcount.
+__global__ void group_check_kernel(const uint32_t* __restrict__ gmask,
+                                   const uint32_t* __restrict__ gstart,
+                                   const uint32_t* __restrict__ d_ng, uint64_t n,
+                                   uint32_t* err) {
     const uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t ng = *d_ng;
     if (g >= ng) return;
     const uint32_t count = (g + 1 < ng ? gstart[g + 1] : (uint32_t)n) - gstart[g];
     if ((uint32_t)__popc(gmask[g]) != count) raise_error(err, TCC_DEVERR_GROUP_DEGREE);
-    const uint32_t w = (uint32_t)(gkey[g] >> ybits);
-    if (w < W) atomicAdd(&wcnt[w], 1u);
 }
 
-__global__ void window_tiles_kernel(const uint32_t* __restrict__ wcnt, uint32_t W,
-                                    uint32_t* __restrict__ tiles) {
+// First group of each window (groups are sorted by window): lower bound of
+// window w in the group keys; wgstart[W] = number of groups.
+__global__ void window_start_kernel(const uint64_t* __restrict__ gkey,
+                                    const uint32_t* __restrict__ d_ng, int ybits, uint32_t W,
+                                    uint32_t* __restrict__ wgstart) {
     const uint32_t w = blockIdx.x * blockDim.x + threadIdx.x;
-    if (w < W) tiles[w] = (wcnt[w] + 7u) / 8u;
+    if (w > W) return;
+    uint32_t lo = 0, hi = *d_ng;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo) / 2;
+        if ((gkey[mid] >> ybits) < w) lo = mid + 1; else hi = mid;
+    }
+    wgstart[w] = lo;
+}
+
+__global__ void window_tiles_kernel(const uint32_t* __restrict__ wgstart, uint32_t W,
+                                    uint32_t* __restrict__ wcnt, uint32_t* __restrict__ tiles) {
+    const uint32_t w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w >= W) return;
+    const uint32_t c = wgstart[w + 1] - wgstart[w];
+    wcnt[w] = c;
+    tiles[w] = (c + 7u) / 8u;
 }
 
 // Padding of each window's last tile: slot / index 0xFFFFFFFF, bitmap byte 0.
@@ -390,12 +406,12 @@ static void build_windows(GroupBuffers& b, uint64_t n, int key_bits, int ybits, 
     } else {
         TCC_CUDA(cudaMemsetAsync(small + 1, 0, 4, s));
     }
-    TCC_CUDA(cudaMemsetAsync(wcnt, 0, (size_t)W * 4, s));
     if (n)
-        window_count_kernel<<<blocks(n), kThreads, 0, s>>>(b.gkey, b.gmask, b.gstart, small + 1,
-                                                           n, ybits, W, wcnt, small + 0);
-    exclusive_scan<uint32_t>(wcnt, wgstart, W, wgstart + W, tmp, s);
-    window_tiles_kernel<<<blocks(W), kThreads, 0, s>>>(wcnt, W, tiles);
+        group_check_kernel<<<blocks(n), kThreads, 0, s>>>(b.gmask, b.gstart, small + 1, n,
+                                                          small + 0);
+    window_start_kernel<<<blocks((uint64_t)W + 1), kThreads, 0, s>>>(b.gkey, small + 1, ybits, W,
+                                                                      wgstart);
+    window_tiles_kernel<<<blocks(W), kThreads, 0, s>>>(wgstart, W, wcnt, tiles);
     exclusive_scan<uint32_t>(tiles, off, W, off + W, tmp, s);
     TCC_CUDA(cudaGetLastError());
 }

@@ -85,17 +85,21 @@ __global__ void plan_fill_kernel(const uint32_t* __restrict__ off, uint32_t W,
     if (n > 1) heavy[atomicAdd(&hdr->heavy_count, 1u)] = w;
 }
 
-// Output rows of windows that several warps reduce into start from zero.
+// Output rows of windows that several warps reduce into start from zero
+// (16-byte stores; F and the row stride are multiples of 4).
 __global__ void zero_heavy_kernel(const uint32_t* __restrict__ heavy,
                                   const PlanHeader* __restrict__ hdr, float* __restrict__ Y,
                                   uint64_t ldy, uint32_t F, uint32_t num_out) {
     const uint32_t n = hdr->heavy_count;
-    for (uint32_t h = blockIdx.x; h < n; h += gridDim.x) {
-        const uint32_t w = heavy[h];
-        for (uint32_t e = threadIdx.x; e < 8 * F; e += blockDim.x) {
-            const uint32_t row = w * 8 + e / F;
-            if (row < num_out) Y[(uint64_t)row * ldy + (e % F)] = 0.f;
-        }
+    const uint32_t q4 = F / 4;
+    const uint32_t per_window = 8 * q4;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (uint64_t)n * per_window;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t h = (uint32_t)(e / per_window);
+        const uint32_t r = (uint32_t)(e % per_window);
+        const uint32_t row = heavy[h] * 8 + r / q4;
+        if (row < num_out) *reinterpret_cast<float4*>(Y + (uint64_t)row * ldy + 4 * (r % q4)) = z;
     }
 }
 
@@ -388,7 +392,8 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
         uint32_t afr[8][4];
         const uint32_t tb = a.win_offset[w], te = a.win_offset[w + 1];
         for (uint32_t t = tb; t < te; ++t) {
-            const uint64_t bm = ld_stream_u64(a.bits + t);
+            uint64_t bm = ld_stream_u64(a.bits + t);
+            if (a.bits_transposed) bm = transpose8x8(bm);
             uint32_t orow = kInvalid;
             uint32_t cslot = 0xFFu;
             if (lane < 8) {

@@ -50,8 +50,9 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
 struct PushTiles {
     uint32_t num_windows;
     const uint32_t* win_offset;
-    const uint64_t* bits;       // bit = outslot*8 + local input
+    const uint64_t* bits;       // bit = outslot*8 + local input (transposed: input*8 + outslot)
     const uint32_t* idx;        // BCSC: output row; SWTCF: super-window row slot
+    bool bits_transposed = false;
     // SWTCF: output row = sw_rows[sw_offset[s] + slot]; repeat cache per super-window
     const uint32_t* sw_offset = nullptr;
     const uint32_t* sw_rows = nullptr;

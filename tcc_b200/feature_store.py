@@ -1,0 +1,75 @@
+"""Hot/cold feature store of the mixed first-layer gather.
+
+Rows of the highest-degree nodes ("hot") live in HBM; the rest ("cold") live in
+pinned host memory that the GPU reads directly (zero-copy over the host link).
+The lookup tables follow the reference's mixed gather
+(cnic/src/core/spmm_kernel.cu:129-153, where cnic/ is
+TAC_training_backend/spmm_cnic/): for condensed column c,
+``g = cache_search_map[c]``; ``g >= 0`` -> row ``g % capacity`` of GPU shard
+``g // capacity``; otherwise row ``id_map[c]`` of the host features.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+
+class FeatureStore:
+    """Features X [num_nodes x F] split by degree into an HBM part and a pinned
+    host part.  ``hot_fraction`` of the nodes (highest degree first) go to HBM."""
+
+    def __init__(self, X: np.ndarray, degrees: np.ndarray, hot_fraction: float = 0.2,
+                 device=None, col_scale: np.ndarray | None = None):
+        """col_scale (optional): a per-node scale folded into the stored rows once,
+        so an aggregation over the store computes A·diag(col_scale)·X."""
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        if col_scale is not None:
+            X = (X * np.asarray(col_scale, dtype=np.float32)[:, None]).astype(np.float32)
+        n, F = X.shape
+        if F % 4:
+            raise ValueError("feature width must be a multiple of 4")
+        n_hot = int(round(hot_fraction * n))
+        order = np.argsort(-degrees.astype(np.int64), kind="stable")
+        hot = np.sort(order[:n_hot])
+        is_hot = np.zeros(n, dtype=bool)
+        is_hot[hot] = True
+        cold = np.nonzero(~is_hot)[0]
+        self.num_nodes, self.F = n, F
+        self.capacity = max(n_hot, 1)
+        csm = np.full(n, -1, dtype=np.int32)
+        csm[hot] = np.arange(n_hot, dtype=np.int32)
+        idm = np.full(n, -1, dtype=np.int32)
+        idm[cold] = np.arange(cold.size, dtype=np.int32)
+        self.cache_search_map = torch.from_numpy(csm).to(device)
+        self.id_map = torch.from_numpy(idm).to(device)
+        self.gpu_rows = torch.from_numpy(X[hot]).to(device) if n_hot else \
+            torch.zeros((1, F), dtype=torch.float32, device=device)
+        self.cpu_rows = torch.from_numpy(X[cold] if cold.size else np.zeros((1, F), np.float32)) \
+            .pin_memory()
+        # device array of per-GPU shard base pointers (one shard on one GPU here)
+        self.gpu_ptrs = torch.tensor([self.gpu_rows.data_ptr()], dtype=torch.int64, device=device)
+        self.n_hot, self.n_cold = n_hot, int(cold.size)
+
+    @property
+    def cpu_ptr(self) -> int:
+        """Device-visible address of the pinned host rows (unified addressing)."""
+        return self.cpu_rows.data_ptr()
+
+    def hot_bytes(self) -> int:
+        return self.n_hot * self.F * 4
+
+    def cold_bytes(self) -> int:
+        return self.n_cold * self.F * 4
+
+    def dense(self) -> torch.Tensor:
+        """All rows gathered into one HBM tensor (for checking)."""
+        out = torch.empty((self.num_nodes, self.F), dtype=torch.float32,
+                          device=self.gpu_rows.device)
+        hot = self.cache_search_map >= 0
+        out[hot] = self.gpu_rows[self.cache_search_map[hot].long()]
+        cold = ~hot
+        out[cold] = self.cpu_rows.to(out.device)[self.id_map[cold].long()]
+        return out

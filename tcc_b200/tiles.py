@@ -187,6 +187,18 @@ def bcsr_spmm(a: Tiles, B: torch.Tensor, C_out: torch.Tensor | None = None,
     return C_out
 
 
+def bcsr_spmm_t(a: Tiles, G: torch.Tensor, Z: torch.Tensor,
+                tc_threshold: int = DEFAULT_TC_THRESHOLD, rs=None, cs=None, stream=None):
+    """Z += diag(cs) A^T diag(rs) G with A as BCSR tiles (push over row windows)."""
+    assert a.kind == "bcsr"
+    _check_f32(G, "G")
+    _check_f32(Z, "Z")
+    s = a.struct()
+    L.call("tcc_bcsr_spmm_t", C.byref(s), _ptr(G), G.stride(0), _ptr(Z), Z.stride(0),
+           G.shape[1], tc_threshold, _ptr(rs), _ptr(cs), _stream(stream))
+    return Z
+
+
 def bcsc_spmm(a: Tiles, B: torch.Tensor, C_out: torch.Tensor,
               tc_threshold: int = DEFAULT_TC_THRESHOLD, rs=None, cs=None, stream=None):
     """C += diag(rs) A diag(cs) B with A as BCSC tiles (push, vector reductions)."""
