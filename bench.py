@@ -9,8 +9,10 @@ fp32 [N x 128] ~ N(0,1).  One step = forward SpMM A.X over BCSR tiles plus the
 transposed SpMM A^T.G over BCSC tiles (the backward pass).  Metric: SpMM
 GFLOP/s = 2 nnz F per SpMM, whole job.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the same per-GPU
-workload (weak scaling, no data-path collective); rank 0 prints the line with
+Multi-GPU (torchrun, one process per GPU): weak scaling -- the R-MAT scale grows
+with log2(N) (about 32 M nonzeros per GPU); the graph is row-partitioned with
+equal nonzeros, each SpMM exchanges the compacted feature halo with an NCCL
+all-to-all overlapped with the local-column tiles; rank 0 prints the line with
 the max time over ranks.
 
 --impl reference: the reference path has no CPU implementation of its own (its
@@ -35,8 +37,9 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-WORKLOAD = ("config2: R-MAT 2^20 nodes, 16M directed edges symmetrised+dedup+self-loops, "
-            "GCN-normalised, F=128, forward A.X (BCSR) + transposed A^T.G (BCSC)")
+WORKLOAD = ("config2 per GPU: R-MAT 2^(20+log2 N) nodes, 16 directed edges per node "
+            "symmetrised+dedup+self-loops, GCN-normalised, F=128, forward A.X + transposed "
+            "A^T.G over BCSR tiles")
 
 
 def parse():
@@ -131,26 +134,43 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_workload(scale, device):
+def build_workload(scale, device, world=1, rank=0, tc_threshold=12):
+    """The rank's share of the R-MAT graph (scale `scale`, 16 * 2^scale directed
+    edges, seed 1, symmetrised + dedup + self-loops; GPU generator), partitioned
+    by nonzeros across `world` ranks, with GCN scales and seeded features."""
     import torch
     from tcc_b200 import graphs as G
-    from tcc_b200 import tiles
+    from tcc_b200.partition import DistGraph, balanced_bounds
     t0 = time.time()
-    g = G.rmat(scale, 16 << scale, seed=1)
-    rs, cs = G.gcn_scales(g)
-    X = G.features(g.cols, 128, seed=1)
-    Gm = G.features(g.rows, 128, seed=11)
-    gen_s = time.time() - t0
-    rp = torch.from_numpy(g.rowptr.view(np.int64)).to(device)
-    col = torch.from_numpy(g.col.view(np.int32)).to(device)
+    rowptr, col, _ = G.rmat_gpu(scale, 16 << scale, seed=1, device=device)
+    deg = torch.diff(rowptr)
+    n = deg.numel()
+    s = torch.where(deg > 0, deg.to(torch.float64).clamp(min=1).rsqrt(),
+                    torch.zeros_like(deg, dtype=torch.float64)).to(torch.float32)
+    bounds = balanced_bounds(deg, world)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    lrp = (rowptr[r0:r1 + 1] - rowptr[r0]).contiguous()
+    lcol = col[rowptr[r0]:rowptr[r1]].contiguous()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    X = torch.randn((r1 - r0, 128), generator=gen, device=device)
+    Gm = torch.randn((r1 - r0, 128), generator=gen, device=device)
     torch.cuda.synchronize()
+    gen_s = time.time() - t0
     t0 = time.time()
-    bcsr = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
-    bcsc = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsc")
+    dg = DistGraph(lrp, lcol, bounds, rs_local=s[r0:r1].contiguous(), cs_global=s,
+                   tc_threshold=tc_threshold)
     torch.cuda.synchronize()
     conv_s = time.time() - t0
-    return dict(g=g, rs=rs, cs=cs, X=X, G=Gm, rp=rp, col=col, bcsr=bcsr, bcsc=bcsc,
-                gen_s=gen_s, conv_s=conv_s)
+    return dict(dg=dg, n=n, bounds=bounds, rowptr=lrp, col=lcol, s=s, X=X, G=Gm,
+                gen_s=gen_s, conv_s=conv_s, full_rowptr=rowptr, full_col=col)
+
+
+def host_csr(rowptr, col, cols):
+    """The device CSR as the oracle's host Csr (uint64 rowptr, uint32 col)."""
+    from tcc_b200 import graphs as G
+    return G.Csr(rowptr.numel() - 1, cols, rowptr.cpu().numpy().astype(np.uint64),
+                 col.cpu().numpy().view(np.uint32))
 
 
 def cpu_baseline(g, X, rs, cs, budget_s=12.0):
@@ -182,31 +202,27 @@ def cpu_baseline(g, X, rs, cs, budget_s=12.0):
 
 
 def run_ours(args, rank, world, local_rank):
+    import math
     import torch
     import torch.distributed as dist
-    from tcc_b200 import tiles
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    W = build_workload(args.scale, device)
-    g, bcsr, bcsc = W["g"], W["bcsr"], W["bcsc"]
-    E, F = g.nnz, 128
-    rs = torch.from_numpy(W["rs"]).to(device)
-    cs = torch.from_numpy(W["cs"]).to(device)
-    X = torch.from_numpy(W["X"]).to(device)
-    Gm = torch.from_numpy(W["G"]).to(device)
-    Y = torch.empty((g.rows, F), device=device)
-    Z = torch.empty((g.cols, F), device=device)
-    thr = args.tc_threshold
+    scale = args.scale + int(round(math.log2(world)))
+    W = build_workload(scale, device, world, rank, args.tc_threshold)
+    dg = W["dg"]
+    F = 128
+    X, Gm = W["X"], W["G"]
+    Y = torch.empty_like(X)
+    Z = torch.empty_like(Gm)
     stream = torch.cuda.current_stream()
 
     def step(fwd_events=None):
         if fwd_events:
             fwd_events[0].record(stream)
-        tiles.bcsr_spmm(bcsr, X, Y, tc_threshold=thr, rs=rs, cs=cs)
+        dg.spmm(X, Y)
         if fwd_events:
             fwd_events[1].record(stream)
-        # transposed pass: Z = diag(cs) A^T diag(rs) G
-        tiles.bcsc_spmm_t(bcsc, Gm, Z, tc_threshold=thr, rs=rs, cs=cs)
+        dg.spmm_t(Gm, Z)  # A^T G: A is symmetric, same partition and tiles
 
     for _ in range(args.warmup):
         step()
@@ -233,18 +249,21 @@ def run_ours(args, rank, world, local_rank):
     ms = e0.elapsed_time(e1)
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd)
     t = torch.tensor([ms, fwd_ms], device=device)
+    tot = torch.tensor([float(dg.nnz), float(dg.halo_rows)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
     ms, fwd_ms = t.tolist()
+    nnz_total, halo_total = tot.tolist()
     ms_per_step = ms / args.steps
-    flops_step = 2 * (2.0 * E * F)
+    flops_step = 2 * (2.0 * nnz_total * F)
 
-    # end to end through the public API: pinned host X, G -> device, both passes,
-    # Y, Z -> pinned host, every step
-    hX = torch.from_numpy(W["X"]).pin_memory()
-    hG = torch.from_numpy(W["G"]).pin_memory()
-    hY = torch.empty((g.rows, F), dtype=torch.float32).pin_memory()
-    hZ = torch.empty((g.cols, F), dtype=torch.float32).pin_memory()
+    # end to end through the public API: pinned-host X, G -> device, both
+    # passes (halo exchange included), Y, Z -> pinned host, every step
+    hX = X.cpu().pin_memory()
+    hG = Gm.cpu().pin_memory()
+    hY = torch.empty_like(hX).pin_memory()
+    hZ = torch.empty_like(hG).pin_memory()
 
     def e2e_step():
         X.copy_(hX, non_blocking=True)
@@ -274,11 +293,13 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return
     peak, peak_kind = measured_peaks()
-    b_alg = 4 * F * (g.rows + g.cols) + 8 * E + 4 * (g.rows + 1)
+    n_loc = dg.n_local
+    b_alg = 4 * F * (n_loc + n_loc) + 8 * dg.nnz + 4 * (n_loc + 1)
     achieved = b_alg / (fwd_ms * 1e-3) / 1e9
+    per_step_launches = 2 * (2 if dg.tiles_halo is None else 4)
     line = {
         "metric": "SpMM GFLOP/s (2*nnz*F)",
-        "value": round(world * flops_step / (ms_per_step * 1e-3) / 1e9, 2),
+        "value": round(flops_step / (ms_per_step * 1e-3) / 1e9, 2),
         "unit": "GFLOP/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -288,46 +309,45 @@ def run_ours(args, rank, world, local_rank):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded R-MAT, numpy PCG64 seed 1)",
-        "config": {"workload": WORKLOAD, "nodes": g.rows, "nnz": E, "F": F,
-                   "tiles_bcsr": bcsr.num_TCBlocks, "tc_threshold": thr,
-                   "l2": "inputs larger than L2 (X, G 512 MiB each)",
-                   "parallelism": f"{world} independent per-GPU replicas" if world > 1 else "1 GPU",
+        "data": "synthetic (seeded R-MAT, torch GPU generator seed 1)",
+        "config": {"workload": WORKLOAD, "rmat_scale": scale, "nodes": W["n"],
+                   "nnz_total": int(nnz_total), "nnz_rank0": dg.nnz, "F": F,
+                   "halo_rows_total": int(halo_total), "tc_threshold": args.tc_threshold,
+                   "l2": "inputs larger than L2 (X, G 512 MiB per GPU)",
+                   "parallelism": (f"{world}-way 1D row partition (nnz-balanced), compacted "
+                                   "halo all-to-all over NCCL overlapped with local tiles")
+                   if world > 1 else "1 GPU",
                    "convert_s": round(W["conv_s"], 3)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": profiled_traffic("pull_kernel_config2"),
-                     "kernel": "pull_kernel (BCSR forward)", "fwd_ms": round(fwd_ms, 4),
-                     "alg_bytes_per_launch": b_alg, "peak_kind": peak_kind},
-        "e2e": {"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
+                     "traffic": profiled_traffic("pull_kernel_config2") if world == 1 else None,
+                     "kernel": "pull_kernel, forward SpMM" + (" (local + halo tiles and the "
+                                                              "exchange)" if world > 1 else ""),
+                     "fwd_ms": round(fwd_ms, 4), "alg_bytes_per_launch": b_alg,
+                     "peak_kind": peak_kind},
+        "e2e": {"value": round(flops_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
                 "h2d_bytes_per_step": int(hX.numel() * 4 + hG.numel() * 4),
                 "d2h_bytes_per_step": int(hY.numel() * 4 + hZ.numel() * 4),
                 "ms_per_step": round(e2e_ms, 3)},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": per_step_launches * args.steps,
         "clocks": clocks,
     }
-    line["cpu_baseline"] = cpu_baseline(g, W["X"], W["rs"], W["cs"])
+    if world == 1:
+        g = host_csr(W["rowptr"], W["col"], W["n"])
+        s = W["s"].cpu().numpy()
+        line["cpu_baseline"] = cpu_baseline(g, X.cpu().numpy(), s, s)
     print(json.dumps(line), flush=True)
 
 
 def run_profile(args):
     import torch
-    from tcc_b200 import tiles
     device = torch.device("cuda", 0)
-    W = build_workload(args.scale, device)
-    g = W["g"]
-    rs = torch.from_numpy(W["rs"]).to(device)
-    cs = torch.from_numpy(W["cs"]).to(device)
-    if args.profile == "fwd":
-        X = torch.from_numpy(W["X"]).to(device)
-        Y = torch.empty((g.rows, 128), device=device)
-        for _ in range(args.steps):
-            tiles.bcsr_spmm(W["bcsr"], X, Y, tc_threshold=args.tc_threshold, rs=rs, cs=cs)
-    else:
-        Gm = torch.from_numpy(W["G"]).to(device)
-        Z = torch.empty((g.cols, 128), device=device)
-        for _ in range(args.steps):
-            tiles.bcsc_spmm_t(W["bcsc"], Gm, Z, tc_threshold=args.tc_threshold, rs=rs, cs=cs)
+    W = build_workload(args.scale, device, tc_threshold=args.tc_threshold)
+    dg = W["dg"]
+    src = W["X"] if args.profile == "fwd" else W["G"]
+    out = torch.empty_like(src)
+    for _ in range(args.steps):
+        dg.spmm(src, out)
     torch.cuda.synchronize()
     print(f"profile {args.profile}: {args.steps} launches done", flush=True)
 
@@ -335,30 +355,40 @@ def run_profile(args):
 def run_reference(args, rank, world, local_rank):
     if rank != 0:
         return
+    import math
+    import torch
     from tcc_b200 import graphs as G
-    g = G.rmat(args.scale, 16 << args.scale, seed=1)
-    rs, cs = G.gcn_scales(g)
-    X = G.features(g.cols, 128, seed=1)
+    scale = args.scale + int(round(math.log2(world)))
+    # the same graph as our arm (torch's CUDA and CPU generators draw different streams)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    rowptr, col, _ = G.rmat_gpu(scale, 16 << scale, seed=1, device=dev)
+    g = host_csr(rowptr, col, rowptr.numel() - 1)
+    del rowptr, col
+    deg = g.degrees().astype(np.float64)
+    s = np.where(deg > 0, 1.0 / np.sqrt(np.maximum(deg, 1)), 0).astype(np.float32)
+    gen = torch.Generator().manual_seed(1000)
+    X = torch.randn((g.rows, 128), generator=gen).numpy()
     for _ in range(args.warmup):
-        cb = cpu_baseline(g, X, rs, cs, budget_s=3.0)
+        cb = cpu_baseline(g, X, s, s, budget_s=3.0)
     vals = []
     for _ in range(args.steps):
-        cb = cpu_baseline(g, X, rs, cs, budget_s=6.0)
+        cb = cpu_baseline(g, X, s, s, budget_s=6.0)
         vals.append(cb["value"])
     value = statistics.median(vals)
     cb["value"] = value
     line = {"impl": "reference", "metric": "SpMM GFLOP/s (2*nnz*F)", "value": value,
             "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded R-MAT, numpy PCG64 seed 1)",
-            "config": {"workload": WORKLOAD, "nodes": g.rows, "nnz": g.nnz, "F": 128},
+            "data": "synthetic (seeded R-MAT, torch generator seed 1)",
+            "config": {"workload": WORKLOAD, "rmat_scale": scale, "nodes": g.rows,
+                       "nnz": g.nnz, "F": 128},
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     try:  # the reference's own CUDA SpMM, built from source for sm_100a (informative)
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
-        if O.ref_lib() is not None:
+        if O.ref_lib() is not None and torch.cuda.is_available():
             dst, src = g.coo()
             _, ms = O.ref_swtcf_spmm(g.rows, g.cols, dst, src, X, tc_threshold=12, warmup=2,
                                      reps=5)

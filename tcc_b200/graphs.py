@@ -218,3 +218,50 @@ def config(idx: int, shrink: int = 0):
         rs, cs = row_scales(g)
         return dict(name=f"rmat-2^{sc}", graph=g, rs=rs, cs=cs, F=128, dist="normal", seed=4)
     raise ValueError(idx)
+
+
+# --------------------------------------------------- GPU (torch) generator --
+
+def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
+             abcd=(0.57, 0.19, 0.19, 0.05), chunk: int = 1 << 26):
+    """R-MAT on the GPU with torch's seeded generator: ``edges`` directed edges on
+    2**scale nodes, symmetrised, deduplicated, self-loops added.
+
+    Every caller with the same (scale, edges, seed) draws the same edges, so each
+    rank of a multi-GPU job can build just its rows: ``row_range = (r0, r1)``
+    keeps rows r0 <= r < r1.  Returns (rowptr int64 [r1-r0+1], col int32 [nnz]
+    global column ids, degrees int64 [2**scale] of the symmetrised multigraph
+    before deduplication + 1 self-loop, used for balancing partitions).
+    """
+    import torch
+    n = 1 << scale
+    r0, r1 = (0, n) if row_range is None else row_range
+    a, b, c, _ = abcd
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    keys = []
+    deg = torch.ones(n, dtype=torch.int64, device=device)  # self-loop
+    for start in range(0, edges, chunk):
+        k = min(chunk, edges - start)
+        u = torch.zeros(k, dtype=torch.int64, device=device)
+        v = torch.zeros(k, dtype=torch.int64, device=device)
+        for level in range(scale):
+            r = torch.rand(k, generator=gen, device=device)
+            bit = 1 << (scale - 1 - level)
+            u += (r >= a + b).to(torch.int64) * bit
+            v += (((r >= a) & (r < a + b)) | (r >= a + b + c)).to(torch.int64) * bit
+        keep = u != v
+        u, v = u[keep], v[keep]
+        deg += torch.bincount(u, minlength=n) + torch.bincount(v, minlength=n)
+        for x, y in ((u, v), (v, u)):
+            m = (x >= r0) & (x < r1)
+            keys.append(((x[m] - r0) << 32) | y[m])
+    loops = torch.arange(r0, r1, dtype=torch.int64, device=device)
+    keys.append(((loops - r0) << 32) | loops)
+    keys = torch.unique(torch.cat(keys))  # sorted, deduplicated
+    rows = (keys >> 32)
+    col = (keys & 0xFFFFFFFF).to(torch.int32)
+    counts = torch.bincount(rows, minlength=r1 - r0)
+    rowptr = torch.zeros(r1 - r0 + 1, dtype=torch.int64, device=device)
+    rowptr[1:] = torch.cumsum(counts, 0)
+    return rowptr, col, deg

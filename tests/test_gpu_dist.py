@@ -1,0 +1,73 @@
+"""Row-partitioned SpMM over NCCL: every rank's rows equal the single-GPU
+result.  Spawns one process per visible GPU (2 or more); skipped otherwise."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-5
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from tcc_b200 import graphs as G
+        from tcc_b200 import tiles
+        from tcc_b200.partition import DistGraph, balanced_bounds
+        dev = torch.device("cuda", rank)
+        rowptr, col, _ = G.rmat_gpu(15, 16 << 15, seed=9, device=dev)
+        deg = torch.diff(rowptr)
+        s = deg.to(torch.float32).clamp(min=1).rsqrt()
+        bounds = balanced_bounds(deg, world)
+        r0, r1 = bounds[rank], bounds[rank + 1]
+        dg = DistGraph((rowptr[r0:r1 + 1] - rowptr[r0]).contiguous(),
+                       col[rowptr[r0]:rowptr[r1]].contiguous(), bounds,
+                       rs_local=s[r0:r1].contiguous(), cs_global=s, tc_threshold=65)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(3)
+        X = torch.randn((deg.numel(), 64), generator=gen, device=dev)  # same X on every rank
+        Y = dg.spmm(X[r0:r1].contiguous())
+        full = tiles.from_csr(rowptr, col, deg.numel(), deg.numel(), kind="bcsr")
+        Yref = tiles.bcsr_spmm(full, X, tc_threshold=65, rs=s, cs=s)[r0:r1]
+        err = (torch.linalg.norm(Y - Yref) / torch.linalg.norm(Yref)).item()
+        torch.cuda.synchronize()
+        q.put((rank, err, dg.halo_rows))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
+def test_row_partitioned_spmm_matches_single_gpu(gpu):
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    for rank, err, halo in res:
+        assert err <= FP32_TOL, (rank, err)
+        assert halo > 0
