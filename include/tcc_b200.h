@@ -50,6 +50,8 @@ typedef int tcc_status;
 #define TCC_DEVERR_HASH_LOOKUP 3
 #define TCC_DEVERR_OCCURRENCE 4    /* row occurrence above the super-window size */
 #define TCC_DEVERR_INDEX_RANGE 5   /* an input index >= rows/cols */
+#define TCC_DEVERR_WAIT_TIMEOUT 6  /* an in-kernel wait for a TMA copy expired (2 s); the
+                                      kernel returned early and its output is incomplete */
 
 const char* tcc_last_error(void);
 const char* tcc_version(void);
@@ -176,6 +178,12 @@ tcc_status tcc_tiles_fill_bcsc(tcc_tiles_workspace* ws, tcc_bcsc* out, cudaStrea
  * caller; pass plan_ready = 1 to reuse a plan built by an earlier call on the
  * same tiling. */
 size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
+/* No counterpart in the reference (its kernels have no bounded waits).  The
+ * pull scratch also holds a device error word: TCC_DEVERR_WAIT_TIMEOUT when a
+ * pull kernel gave up waiting for one of its TMA copies.  Synchronises
+ * `stream`, stores the word in *code and clears it.  The word is also cleared
+ * whenever a call builds the plan (plan_ready = 0). */
+tcc_status tcc_pull_device_error(void* scratch, int* code, cudaStream_t stream);
 
 /* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
  * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):

@@ -379,6 +379,18 @@ size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
     return tcc::pull_scratch_bytes(num_windows, num_tiles);
 }
 
+tcc_status tcc_pull_device_error(void* scratch, int* code, cudaStream_t stream) {
+    return guarded("tcc_pull_device_error", [&] {
+        TCC_REQUIRE(scratch && code, "scratch and code must not be NULL");
+        uint32_t* word = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + tcc::kPullErrorOffset);
+        uint32_t v = 0;
+        TCC_CUDA(cudaMemcpyAsync(&v, word, sizeof(v), cudaMemcpyDeviceToHost, stream));
+        TCC_CUDA(cudaMemsetAsync(word, 0, sizeof(v), stream));
+        TCC_CUDA(cudaStreamSynchronize(stream));
+        *code = (int)v;
+    });
+}
+
 tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float* C, uint64_t ldc,
                          uint32_t F, uint32_t tc_threshold, const float* rs, const float* cs,
                          int accumulate, void* scratch, size_t scratch_bytes, int plan_ready,

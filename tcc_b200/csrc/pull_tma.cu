@@ -1,0 +1,449 @@
+// pull_tma.cu -- bulk-copy gather pull SpMM (BCSR forward, BCSC transposed) on sm_100a.
+//
+// Same arithmetic contract as the owner-computes pull pass (window w owns
+// output rows 8w..8w+7; cnic BCSR kernel, cnic/src/core/spmm_kernel.cu:
+// 1560-1843, and the transposed pass that replaces torch.sparse.mm(A_topo.T, .)
+// at train/tcgnn_conv_release.py:152), with a different data path:
+//
+// * Work split: the tile range [0, T) is cut into G equal pieces, one per warp
+//   (G = CTAs x warps).  A warp walks the windows that meet its piece in order
+//   and keeps the window's 8 x F-slice partial sums in registers, so a window
+//   is written once with plain stores.  Windows cut by a piece boundary, and
+//   windows longer than kFlushTiles tiles (whose warp flushes every
+//   kFlushTiles tiles to keep fp32 sums short), are zeroed first and reduced
+//   with red.global.add.v4.
+// * Gathers: each real feature row of a tile (up to 8 x 512 B) is fetched by
+//   one bulk async copy (the TMA unit's cp.async.bulk) into a per-warp ring of
+//   kR shared-memory stages completed through mbarriers.  This keeps the row
+//   gathers off the LSU/L1 fill path, where every missed 32-byte sector costs
+//   a data-pipe wavefront.  Rows sit 32 bytes apart beyond their length, so
+//   the MMA fragment loads (4 rows x 8 float4 per quarter-warp) hit 8 distinct
+//   bank groups.
+// * Arithmetic: the tensor-core tile product of tile_mma_scaled -- TF32 for
+//   tiles with popcount >= tc_threshold (the reference's dense-tile
+//   arithmetic), an fp32-level TF32 split for the others -- with the column
+//   scale folded into the B operand.
+// * Metadata (gather indices, bitmaps, column scales) runs three 16-tile
+//   batches ahead in registers, so neither the index stream nor the dependent
+//   scale loads stall the warp.
+//
+// Every mbarrier wait is bounded by %globaltimer; on expiry the kernel records
+// TCC_DEVERR_WAIT_TIMEOUT, waits (bounded) for its own copies in flight
+// and returns.
+#include "spmm.cuh"
+#include "tile_mma.cuh"
+
+#include <cstddef>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+namespace tcc {
+
+namespace {
+
+constexpr int kTW = 12;                          // warps per CTA
+constexpr int kR = 4;                            // ring stages per warp
+constexpr uint32_t kMaxBox = 128;                // floats per gathered row segment
+constexpr uint32_t kRowPad = 32;                 // bytes between rows beyond their length
+constexpr uint32_t kStageBytes = 8 * (kMaxBox * 4 + kRowPad);
+constexpr uint32_t kBatch = 16;                  // tiles per metadata batch
+constexpr uint32_t kFlushTiles = 64;             // max tiles summed in one fp32 register chain
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+struct __align__(16) StageMeta {
+    float cs[8];              // column scale of gathered row k (0 for padding); 16-byte stores
+    unsigned long long bits;  // output-major bitmap: bit r*8 + k
+    uint32_t valid;           // bit k: gathered row k holds a real column (others are stale)
+    uint32_t pad[5];
+};
+static_assert(sizeof(StageMeta) == 64 && offsetof(StageMeta, cs) == 0,
+              "stage metadata: 64 bytes, column scales 16-byte aligned");
+
+constexpr size_t kSmemBytes =
+    (size_t)kTW * kR * (kStageBytes + sizeof(StageMeta) + sizeof(uint64_t)) + 1024;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of the mbarrier; false after kWaitNs.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        if (mbar_try(bar, parity)) return true;
+        if (globaltimer() - t0 > kWaitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+// One contiguous global -> shared copy by the TMA unit, completing on `bar`
+// (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const uint32_t* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_nc_u64(const uint64_t* p) {
+    unsigned long long v;
+    asm volatile("ld.global.nc.L1::no_allocate.u64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
+
+// First i in [lo, hi) with pred(i), hi if none (pred monotone false -> true);
+// 32-way search over the warp, result uniform.
+template <class P>
+__device__ __forceinline__ uint32_t warp_lower_bound(uint32_t lo, uint32_t hi, P pred, int lane) {
+    // invariant: the answer lies in [lo, hi]; hi is either the original
+    // bound or an index already known to satisfy pred
+    while (hi - lo > 32) {
+        const uint32_t step = (hi - lo + 31) / 32;
+        const uint32_t p = lo + lane * step;
+        const bool tested = p < hi;
+        const unsigned b = __ballot_sync(0xffffffffu, tested && pred(p));
+        if (b == 0) {
+            const unsigned tm = __ballot_sync(0xffffffffu, tested);
+            lo += (31 - __clz(tm)) * step + 1;  // past the last tested probe
+        } else {
+            const int f = __ffs(b) - 1;
+            hi = lo + f * step;
+            if (f > 0) lo += (f - 1) * step + 1;
+        }
+    }
+    const uint32_t p = lo + lane;
+    const unsigned b = __ballot_sync(0xffffffffu, p < hi && pred(p));
+    return b ? lo + __ffs(b) - 1 : hi;
+}
+
+// Metadata of one 16-tile batch as held by a lane: tile base + lane/2, gather
+// rows 4*(lane&1) .. +3.
+struct Batch {
+    uint4 idx;
+    unsigned long long bits;
+    float4 cs;
+};
+
+// Window w is "reduced" -- its rows are written with red.global.add into rows
+// zeroed here -- when a warp-piece boundary T_g = floor(g*T/G) (0 < g < G)
+// falls strictly inside its tiles, or when it has more than kFlushTiles tiles
+// (its warp flushes every kFlushTiles tiles to keep fp32 sums short).  The
+// kernel's own test is the same: o0 < T0 || o1 > T1 || o1 - o0 > kFlushTiles.
+__device__ __forceinline__ bool window_reduced(uint32_t o0, uint32_t o1, uint32_t T, uint32_t G) {
+    if (o1 - o0 > kFlushTiles) return true;
+    if (T == 0 || o1 - o0 < 2) return false;
+    // smallest g with floor(g*T/G) > o0
+    const uint64_t g = ((uint64_t)(o0 + 1) * G + T - 1) / T;
+    return g < G && (uint64_t)g * T / G < o1;
+}
+
+__global__ void zero_reduced_kernel(const uint32_t* __restrict__ off, uint32_t W, uint32_t T,
+                                    uint32_t G, float* __restrict__ Y, uint64_t ldy, uint32_t F,
+                                    uint32_t num_out) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t q4 = F / 4;
+    for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < W;
+         w += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
+        if (!window_reduced(off[w], off[w + 1], T, G)) continue;
+        for (uint32_t e = lane; e < 8 * q4; e += 32) {
+            const uint64_t row = w * 8 + e / q4;
+            if (row < num_out)
+                *reinterpret_cast<float4*>(Y + row * ldy + 4 * (e % q4)) =
+                    make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+
+template <int NP>
+__global__ void __launch_bounds__(kTW * 32, 1)
+    pull_tma_kernel(PullTiles a, Dense d, uint32_t bw, uint32_t thr, int accumulate,
+                    uint32_t* __restrict__ err) {
+    extern __shared__ unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
+    // 1024-byte aligned base (TMA destinations need 128)
+    const uint32_t raw = smem_u32(smem_raw);
+    unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    unsigned char* sdata = smem + (size_t)wib * kR * kStageBytes;
+    StageMeta* smeta = reinterpret_cast<StageMeta*>(smem + (size_t)kTW * kR * kStageBytes) + wib * kR;
+    uint64_t* sbar = reinterpret_cast<uint64_t*>(smem + (size_t)kTW * kR * (kStageBytes + sizeof(StageMeta))) +
+                     wib * kR;
+
+    if (lane < kR) mbar_init(smem_u32(&sbar[lane]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncwarp();
+
+    const uint32_t rowbytes = bw * 4;
+    const uint32_t pitch = rowbytes + kRowPad;
+    const int32_t fb = (int32_t)(blockIdx.y * kMaxBox);
+    const int gid = lane >> 2, tig = lane & 3;
+    const uint64_t G = (uint64_t)gridDim.x * kTW;
+    const uint64_t g = (uint64_t)blockIdx.x * kTW + wib;
+    const uint32_t T = a.num_tiles, W = a.num_windows;
+    const uint32_t T0 = (uint32_t)(g * T / G), T1 = (uint32_t)((g + 1) * T / G);
+    const uint32_t* off = a.win_offset;
+
+    // windows meeting [T0, T1): first w with off[w+1] > T0 or off[w] >= T0,
+    // up to the first window starting at or after T1 (all remaining for the
+    // last warp, so trailing empty windows are written)
+    const uint32_t wb = warp_lower_bound(
+        0, W, [&](uint32_t w) { return off[w + 1] > T0 || off[w] >= T0; }, lane);
+    const uint32_t we =
+        g + 1 == G ? W : warp_lower_bound(wb, W, [&](uint32_t w) { return off[w] >= T1; }, lane);
+
+    // ---- metadata pipeline: B0 current (complete), B1 (cs in flight), B2 (idx in flight)
+    auto load_idx = [&](uint32_t base, Batch& b) {
+        const uint32_t t = base + (lane >> 1);
+        b.idx = make_uint4(kInvalid, kInvalid, kInvalid, kInvalid);
+        b.bits = 0;
+        if (t < T1) {
+            b.idx = ld_nc_v4(a.idx + (uint64_t)t * 8 + 4 * (lane & 1));
+            b.bits = ld_nc_u64(a.bits + t);
+        }
+    };
+    auto load_cs = [&](Batch& b) {
+        auto one = [&](uint32_t k) {
+            return k < a.num_in ? (d.cs ? __ldg(d.cs + k) : 1.f) : 0.f;
+        };
+        b.cs = make_float4(one(b.idx.x), one(b.idx.y), one(b.idx.z), one(b.idx.w));
+    };
+    // bitmap to output-major form, padding columns cleared; returns the
+    // tile's valid-row mask (bit k: gather row k is a real column)
+    auto finish = [&](Batch& b) -> uint32_t {
+        unsigned long long bits = b.bits;
+        if (a.bits_transposed) bits = transpose8x8(bits);
+        const uint32_t n_in = a.num_in;
+        uint32_t vmask = (b.idx.x < n_in ? 1u : 0u) | (b.idx.y < n_in ? 2u : 0u) |
+                         (b.idx.z < n_in ? 4u : 0u) | (b.idx.w < n_in ? 8u : 0u);
+        vmask <<= 4 * (lane & 1);
+        vmask |= __shfl_xor_sync(0xffffffffu, vmask, 1);
+        b.bits = bits & (0x0101010101010101ull * (unsigned long long)vmask);
+        return vmask;
+    };
+
+    Batch B0, B1, B2;
+    uint32_t vmask = 0;
+    uint32_t mb = T0;
+    if (T0 < T1) {
+        load_idx(T0, B0);
+        load_idx(T0 + kBatch, B1);
+        load_idx(T0 + 2 * kBatch, B2);
+        load_cs(B0);
+        load_cs(B1);
+        vmask = finish(B0);
+    }
+
+    auto issue = [&](uint32_t t) {
+        if (t >= mb + kBatch) {  // rotate (uniform: t is the same in every lane)
+            B0 = B1;
+            B1 = B2;
+            mb += kBatch;
+            load_cs(B1);
+            load_idx(mb + 2 * kBatch, B2);
+            vmask = finish(B0);
+        }
+        const uint32_t j = t - mb;
+        if ((uint32_t)(lane >> 1) == j) {
+            const uint32_t q = (t - T0) % kR;
+            const uint32_t bar = smem_u32(&sbar[q]);
+            const int h = lane & 1;
+            StageMeta& m = smeta[q];
+            if (h == 0) {
+                m.bits = B0.bits;
+                m.valid = vmask;
+                *reinterpret_cast<float4*>(&m.cs[0]) = B0.cs;
+            } else {
+                *reinterpret_cast<float4*>(&m.cs[4]) = B0.cs;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (h == 0) mbar_arrive_tx(bar, (uint32_t)__popc(vmask) * rowbytes);
+            // real rows of this lane's half; padding rows are not fetched
+            const uint32_t dst = smem_u32(sdata + q * kStageBytes) + 4 * h * pitch;
+            const uint32_t rows[4] = {B0.idx.x, B0.idx.y, B0.idx.z, B0.idx.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if ((vmask >> (4 * h + e)) & 1u)
+                    bulk_copy(dst + e * pitch, d.X + (uint64_t)rows[e] * d.ldx + fb, rowbytes, bar);
+        }
+    };
+
+    // window offsets, 32 at a time
+    uint32_t ob = wb;
+    uint32_t offv = wb + lane <= W ? off[wb + lane] : 0;
+    auto off_at = [&](uint32_t i) -> uint32_t {  // uniform i, ob <= i < ob + 32
+        return __shfl_sync(0xffffffffu, offv, (int)(i - ob));
+    };
+
+    uint32_t t = T0;
+    for (uint32_t p = T0; p < T1 && p < T0 + kR; ++p) issue(p);
+    __syncwarp();  // stage metadata written by the issuing lanes
+
+    // Write (or reduce) a window's partial sums: lane holds output rows 2tig,
+    // 2tig+1 at float4 slots gid + 8s.  rsv: lane r < 8 holds rs of row r.
+    uint32_t row0 = 0;
+    float rsv = 1.f;
+    auto emit = [&](float (&acc)[4 * NP][4], bool red) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float rsc = __shfl_sync(0xffffffffu, rsv, 2 * tig + h);
+            const uint32_t row = row0 + 2 * tig + h;
+            if (row >= a.num_out) continue;
+            float* yrow = d.Y + (uint64_t)row * d.ldy + fb;
+#pragma unroll
+            for (int sl = 0; sl < 2 * NP; ++sl) {
+                const uint32_t f = 4 * (gid + 8 * sl);
+                if (f >= bw) continue;
+                const int p = sl >> 1, e = (sl & 1) * 2 + h;
+                float4 v = make_float4(acc[4 * p + 0][e], acc[4 * p + 1][e], acc[4 * p + 2][e],
+                                       acc[4 * p + 3][e]);
+                v = f4_scale(v, rsc);
+                float* yp = yrow + f;
+                if (red) {
+                    red_add_v4(yp, v);
+                } else if (accumulate) {
+                    *reinterpret_cast<float4*>(yp) = f4_add(*reinterpret_cast<const float4*>(yp), v);
+                } else {
+                    __stcs(reinterpret_cast<float4*>(yp), v);
+                }
+            }
+        }
+    };
+
+    bool failed = false;
+    for (uint32_t w = wb; w < we && !failed; ++w) {
+        if (w + 1 >= ob + 32) {
+            ob = w;
+            offv = ob + lane <= W ? off[ob + lane] : 0;
+        }
+        const uint32_t o0 = off_at(w), o1 = off_at(w + 1);
+        const uint32_t te = min(o1, T1);
+        const bool reduced = o0 < T0 || o1 > T1 || o1 - o0 > kFlushTiles;
+        row0 = w * 8;
+        rsv = (d.rs && lane < 8 && row0 + lane < a.num_out) ? __ldg(d.rs + row0 + lane) : 1.f;
+        uint32_t chain = 0;
+
+        float dacc[4 * NP][4];
+#pragma unroll
+        for (int j = 0; j < 4 * NP; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
+
+        for (; t < te; ++t) {
+            const uint32_t q = (t - T0) % kR;
+            const uint32_t par = ((t - T0) / kR) & 1u;
+            bool ok = mbar_try(smem_u32(&sbar[q]), par);
+            if (!__all_sync(0xffffffffu, ok)) ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sbar[q]), par));
+            if (!ok) {
+                failed = true;
+                break;
+            }
+            const StageMeta& m = smeta[q];
+            const unsigned long long bits = m.bits;
+            const uint32_t valid = m.valid;
+            const float c0 = m.cs[tig], c1 = m.cs[tig + 4];
+            const unsigned char* src = sdata + q * kStageBytes;
+            // fragment-order rows k = tig + 4r, float4 slots 4*(gid + 8s) (tile_mma)
+            float4 x[2][2 * NP];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int k = tig + 4 * r;
+                // rows of padding columns were never written: zero them, or
+                // 0 * NaN could reach the accumulators
+                const bool ok = (valid >> k) & 1u;
+#pragma unroll
+                for (int sl = 0; sl < 2 * NP; ++sl) {
+                    const uint32_t f = 4 * (gid + 8 * sl);
+                    x[r][sl] = ok && f < bw ? *reinterpret_cast<const float4*>(src + k * pitch + 4 * f)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            __syncwarp();
+            if (t + kR < T1) issue(t + kR);
+            tile_mma_scaled<NP>(dacc, x, bits, c0, c1, gid, tig, (uint32_t)__popcll(bits) < thr,
+                                d.cs != nullptr);
+            if (++chain == kFlushTiles && t + 1 < te) {  // reduced windows only
+                emit(dacc, true);
+#pragma unroll
+                for (int j = 0; j < 4 * NP; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
+                chain = 0;
+            }
+        }
+        if (failed) break;
+
+        emit(dacc, reduced);
+    }
+
+    if (failed) {
+        if (lane == 0) atomicExch(err, (uint32_t)TCC_DEVERR_WAIT_TIMEOUT);
+        // copies still in flight: tiles issued (t .. min(T1, t+kR)) not consumed
+        for (uint32_t u = t; u < T1 && u < t + kR; ++u) {
+            const uint32_t q = (u - T0) % kR;
+            (void)mbar_wait(smem_u32(&sbar[q]), ((u - T0) / kR) & 1u);
+        }
+    }
+}
+
+}  // namespace
+
+bool pull_tma_eligible(const PullTiles& a, const Dense& d) {
+    // opt-in (TCC_PULL_KERNEL=tma): measured slower than the register-gather
+    // kernel on the power-law configs (instruction-bound, ~345 instructions
+    // per tile against ~250)
+    const char* e = std::getenv("TCC_PULL_KERNEL");
+    if (!e || std::strcmp(e, "tma") != 0 || a.sw_rows) return false;
+    if (d.F % 4 != 0 || (d.F > kMaxBox && d.F % kMaxBox != 0)) return false;
+    if (a.num_in == 0) return false;
+    return (uintptr_t)d.X % 16 == 0 && d.ldx % 4 == 0;
+}
+
+void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, uint32_t* err,
+              cudaStream_t s) {
+    const uint32_t bw = d.F <= kMaxBox ? d.F : kMaxBox;
+    const uint32_t slices = d.F <= kMaxBox ? 1 : d.F / kMaxBox;
+    const uint32_t ctas = (uint32_t)sm_count();
+    const uint32_t G = ctas * kTW;
+    if (!accumulate && a.num_tiles > 0)
+        zero_reduced_kernel<<<std::min<unsigned>(ceil_div(a.num_windows, 8), ctas * 8), 256, 0, s>>>(
+            a.win_offset, a.num_windows, a.num_tiles, G, d.Y, d.ldy, d.F, a.num_out);
+    auto k = bw <= 64 ? pull_tma_kernel<1> : pull_tma_kernel<2>;
+    TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(a, d, bw, thr, accumulate, err);
+    TCC_CUDA(cudaGetLastError());
+}
+
+}  // namespace tcc

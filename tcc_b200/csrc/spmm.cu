@@ -19,7 +19,9 @@
 // 246-264).
 #include "spmm.cuh"
 #include "primitives.cuh"
+#include "tile_mma.cuh"
 
+#include <cstddef>
 #include <mutex>
 
 namespace tcc {
@@ -40,7 +42,6 @@ namespace {
 constexpr uint32_t kChunkTiles = 16;  // max tiles per warp task
 constexpr int kPushWarps = 4;         // warps per push block
 constexpr int kStage = 136;           // floats per staged 128-feature row (bank-conflict free)
-constexpr uint32_t kOne = 0x3f800000u;
 
 struct PlanHeader {
     uint32_t num_chunks;
@@ -118,61 +119,6 @@ __device__ __forceinline__ const float* store_row(const FeatureStore& fs, uint32
         return base + (uint64_t)(g % fs.gpu_capacity) * F;
     }
     return fs.cpu_features + (uint64_t)fs.id_map[c] * F;
-}
-
-__device__ __forceinline__ float comp(const float4& v, int c) {
-    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
-}
-
-// Tile MMAs of one 8x8 tile.  The warp's 64*NP features are permuted across
-// MMA slots so that each lane's float4 gathers feed the A fragments directly:
-// MMA j = 4p + c, slot m holds feature 4*(m + 16p) + c.  Lane (gid, tig) holds
-// x[r][s] = X[gather row k = tig + 4r][4*(gid + 8s) .. +3]; B[k][n] = bit(n*8+k).
-// pass2 == false: one TF32 pass with operands rounded like cvt.rna (the
-// reference's dense-tile arithmetic).  pass2 == true: fp32-accurate split
-// x = hi + lo (hi = x with the low 13 bits cleared, exact), all hi MMAs
-// first, then all lo MMAs.
-template <int NP>
-__device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 (&x)[2][2 * NP],
-                                         uint64_t bm, int gid, int tig, bool pass2) {
-    uint32_t b[2];
-    b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
-    b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
-    if (!pass2) {
-#pragma unroll
-        for (int p = 0; p < NP; ++p)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint32_t a[4] = {tf32_rna_bits(comp(x[0][2 * p], c)), tf32_rna_bits(comp(x[0][2 * p + 1], c)),
-                                       tf32_rna_bits(comp(x[1][2 * p], c)), tf32_rna_bits(comp(x[1][2 * p + 1], c))};
-                mma_tf32_16x8x8(dacc[4 * p + c], a, b);
-            }
-        return;
-    }
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t hi[4] = {
-                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
-            mma_tf32_16x8x8(dacc[4 * p + c], hi, b);
-        }
-    // lo = x - hi is exact in fp32; recomputed here to keep registers free
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const float v[4] = {comp(x[0][2 * p], c), comp(x[0][2 * p + 1], c),
-                                comp(x[1][2 * p], c), comp(x[1][2 * p + 1], c)};
-            uint32_t lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                lo[e] = __float_as_uint(v[e] - __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
-            mma_tf32_16x8x8(dacc[4 * p + c], lo, b);
-        }
 }
 
 // ---------------------------------------------------------------- pull ----
@@ -538,6 +484,11 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
         plan_count_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart);
         exclusive_scan<uint32_t>(cstart, cstart, W, cstart + W, base + L.tmp, s);
         plan_fill_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart, desc, heavy, hdr);
+    }
+    static_assert(offsetof(PlanHeader, pad) == kPullErrorOffset, "error word offset");
+    if (!fs && pull_tma_eligible(a, d)) {
+        pull_tma(a, d, tc_threshold, accumulate, &hdr->pad[0], s);
+        return;
     }
     if (!accumulate)
         zero_heavy_kernel<<<std::max(1, sm_count() * 2), 256, 0, s>>>(heavy, hdr, d.Y, d.ldy, d.F,

@@ -46,6 +46,14 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
                void* scratch, size_t scratch_bytes, bool plan_ready, const FeatureStore* fs,
                cudaStream_t s);
 
+// Bulk-copy gather pull kernel (pull_tma.cu): BCSR forward / BCSC transposed over
+// a dense X; F a multiple of 4 and either <= 128 or a multiple of 128.
+bool pull_tma_eligible(const PullTiles& a, const Dense& d);
+void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, uint32_t* err,
+              cudaStream_t s);
+// Offset of the device error word inside a pull scratch.
+constexpr size_t kPullErrorOffset = 8;
+
 // Tile source of a push pass (window w owns inputs 8w..8w+7 and scatters).
 struct PushTiles {
     uint32_t num_windows;

@@ -1,0 +1,133 @@
+// tile_mma.cuh -- one 8x8 window tile times a 64*NP-feature slice on the
+// TF32 tensor cores (mma.sync m16n8k8), shared by the pull kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace tcc {
+
+constexpr uint32_t kOne = 0x3f800000u;  // 1.0f
+
+__device__ __forceinline__ float comp(const float4& v, int c) {
+    return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+}
+
+// Tile MMAs of one 8x8 tile.  The warp's 64*NP features are permuted across
+// MMA slots so that each lane's float4 gathers feed the A fragments directly:
+// MMA j = 4p + c, slot m holds feature 4*(m + 16p) + c.  Lane (gid, tig) holds
+// x[r][s] = X[gather row k = tig + 4r][4*(gid + 8s) .. +3]; B[k][n] = bit(n*8+k).
+// pass2 == false: one TF32 pass with operands rounded like cvt.rna (the
+// reference's dense-tile arithmetic).  pass2 == true: fp32-accurate split
+// x = hi + lo (hi = x with the low 13 bits cleared, exact), all hi MMAs
+// first, then all lo MMAs.
+template <int NP>
+__device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 (&x)[2][2 * NP],
+                                         uint64_t bm, int gid, int tig, bool pass2) {
+    uint32_t b[2];
+    b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
+    b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
+    if (!pass2) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t a[4] = {tf32_rna_bits(comp(x[0][2 * p], c)), tf32_rna_bits(comp(x[0][2 * p + 1], c)),
+                                       tf32_rna_bits(comp(x[1][2 * p], c)), tf32_rna_bits(comp(x[1][2 * p + 1], c))};
+                mma_tf32_16x8x8(dacc[4 * p + c], a, b);
+            }
+        return;
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t hi[4] = {
+                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
+            mma_tf32_16x8x8(dacc[4 * p + c], hi, b);
+        }
+    // lo = x - hi is exact in fp32; recomputed here to keep registers free
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float v[4] = {comp(x[0][2 * p], c), comp(x[0][2 * p + 1], c),
+                                comp(x[1][2 * p], c), comp(x[1][2 * p + 1], c)};
+            uint32_t lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                lo[e] = __float_as_uint(v[e] - __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
+            mma_tf32_16x8x8(dacc[4 * p + c], lo, b);
+        }
+}
+
+// tile_mma with the column scale folded into B: B[k][n] = bit(n*8+k) ? c_k : 0,
+// x holds the unscaled rows (zeros for padding rows).  Lane (gid, tig) passes
+// c0 = scale of gather row tig, c1 = of row tig + 4.
+// pass2 == false: one TF32 pass, A and B rounded like cvt.rna.
+// pass2 == true: fp32-level split -- a = a_hi + a_lo, b = b_hi + b_lo (hi: low
+// 13 bits cleared, exact in TF32) and D += a_hi*b_hi + a_lo*b_hi (+ a_hi*b_lo
+// when `scaled`; with unit scales b_lo is 0).  The dropped a_lo*b_lo term is
+// below 2^-20 relative.
+template <int NP>
+__device__ __forceinline__ void tile_mma_scaled(float (&dacc)[4 * NP][4],
+                                                const float4 (&x)[2][2 * NP], uint64_t bm,
+                                                float c0, float c1, int gid, int tig, bool pass2,
+                                                bool scaled) {
+    const float bf0 = ((bm >> (gid * 8 + tig)) & 1ull) ? c0 : 0.f;
+    const float bf1 = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? c1 : 0.f;
+    if (!pass2) {
+        const uint32_t b[2] = {tf32_rna_bits(bf0), tf32_rna_bits(bf1)};
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t a[4] = {tf32_rna_bits(comp(x[0][2 * p], c)), tf32_rna_bits(comp(x[0][2 * p + 1], c)),
+                                       tf32_rna_bits(comp(x[1][2 * p], c)), tf32_rna_bits(comp(x[1][2 * p + 1], c))};
+                mma_tf32_16x8x8(dacc[4 * p + c], a, b);
+            }
+        return;
+    }
+    const uint32_t bh[2] = {__float_as_uint(bf0) & 0xFFFFE000u, __float_as_uint(bf1) & 0xFFFFE000u};
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t hi[4] = {
+                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
+            mma_tf32_16x8x8(dacc[4 * p + c], hi, bh);
+        }
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float v[4] = {comp(x[0][2 * p], c), comp(x[0][2 * p + 1], c),
+                                comp(x[1][2 * p], c), comp(x[1][2 * p + 1], c)};
+            uint32_t lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                lo[e] = __float_as_uint(v[e] - __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
+            mma_tf32_16x8x8(dacc[4 * p + c], lo, bh);
+        }
+    if (!scaled) return;
+    const uint32_t bl[2] = {__float_as_uint(bf0 - __uint_as_float(bh[0])),
+                            __float_as_uint(bf1 - __uint_as_float(bh[1]))};
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t hi[4] = {
+                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
+                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
+            mma_tf32_16x8x8(dacc[4 * p + c], hi, bl);
+        }
+}
+
+}  // namespace tcc

@@ -187,6 +187,17 @@ def bcsr_spmm(a: Tiles, B: torch.Tensor, C_out: torch.Tensor | None = None,
     return C_out
 
 
+def pull_device_error(a: Tiles, stream=None) -> int:
+    """Device error word of the tiling's pull scratch (0, or
+    TCC_DEVERR_WAIT_TIMEOUT when a pull kernel gave up waiting on one of its
+    TMA copies); synchronises the stream and clears the word."""
+    if a._scratch is None:
+        return 0
+    code = C.c_int(0)
+    L.call("tcc_pull_device_error", _ptr(a._scratch), C.byref(code), _stream(stream))
+    return code.value
+
+
 def bcsr_spmm_t(a: Tiles, G: torch.Tensor, Z: torch.Tensor,
                 tc_threshold: int = DEFAULT_TC_THRESHOLD, rs=None, cs=None, stream=None):
     """Z += diag(cs) A^T diag(rs) G with A as BCSR tiles (push over row windows)."""

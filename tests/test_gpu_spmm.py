@@ -113,10 +113,22 @@ def test_swtcf_transposed(gpu, oracle, name, g, F):
     assert rel_fro(Z2.cpu().numpy(), oracle.csr_spmm_t(g, Gm)) <= TF32_TOL
 
 
+@pytest.fixture(params=["tma", "ldg"])
+def pull_kernel(request, monkeypatch):
+    """Run a pull test on the register-gather kernel (default) and on the
+    bulk-copy gather kernel (TCC_PULL_KERNEL=tma); F that the bulk-copy kernel
+    does not take falls back to the register-gather kernel either way."""
+    if request.param == "tma":
+        monkeypatch.setenv("TCC_PULL_KERNEL", "tma")
+    else:
+        monkeypatch.delenv("TCC_PULL_KERNEL", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("name,g", CASES, ids=[c[0] for c in CASES])
 @pytest.mark.parametrize("F,thr", [(128, 65), (128, 12), (128, 0), (4, 65), (32, 65), (64, 65),
-                                   (100, 12), (256, 12), (512, 65), (48, 0)])
-def test_bcsr_pull(gpu, oracle, name, g, F, thr):
+                                   (100, 12), (256, 12), (512, 65), (48, 0), (8, 0), (384, 12)])
+def test_bcsr_pull(gpu, oracle, pull_kernel, name, g, F, thr):
     rp, col = csr_dev(g)
     t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
     rs, cs = G.gcn_scales(g) if g.rows == g.cols else G.row_scales(g)
@@ -131,9 +143,10 @@ def test_bcsr_pull(gpu, oracle, name, g, F, thr):
     assert rel_fro(Y2.cpu().numpy(), 2 * want) <= (FP32_TOL if thr > 64 else TF32_TOL)
 
 
-def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle):
+def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle, pull_kernel):
     """TF32 on every tile (the cnic reference arithmetic) vs the oracle's tile
-    restatement of it."""
+    restatement of it, on both pull kernels; the TMA kernel's device error
+    word stays clear."""
     g = G.sbm(2000, 20, 120000, 40.0, 1.2, seed=12)
     rp, col = csr_dev(g)
     t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
@@ -141,11 +154,14 @@ def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle):
     Y = tiles.bcsr_spmm(t, dense(X), tc_threshold=0)
     want = oracle.bcsr_spmm(oracle.bcsr_from_csr(g), X, tc_threshold=0)
     assert rel_fro(Y.cpu().numpy(), want) <= FP32_TOL
+    Y65 = tiles.bcsr_spmm(t, dense(X), tc_threshold=65)
+    assert rel_fro(Y65.cpu().numpy(), oracle.csr_spmm(g, X)) <= FP32_TOL
+    assert tiles.pull_device_error(t) == 0
 
 
 @pytest.mark.parametrize("name,g", CASES, ids=[c[0] for c in CASES])
 @pytest.mark.parametrize("F,thr", [(128, 65), (128, 0), (64, 12), (256, 65)])
-def test_bcsc_push_and_transposed(gpu, oracle, name, g, F, thr):
+def test_bcsc_push_and_transposed(gpu, oracle, pull_kernel, name, g, F, thr):
     rp, col = csr_dev(g)
     t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsc")
     X = G.features(g.cols, F, seed=10)
