@@ -267,6 +267,13 @@ def tf32(x):
     return r.view(np.float32)
 
 
+def tf32_trunc(x):
+    """fp32 -> TF32 by dropping the low 13 mantissa bits: how the tcgen05
+    kind::tf32 tensor-core MMA reads an fp32 operand from shared memory."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
 # -------------------------------------------------------------- reference --
 
 def ref_lib():

@@ -486,6 +486,10 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
         plan_fill_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart, desc, heavy, hdr);
     }
     static_assert(offsetof(PlanHeader, pad) == kPullErrorOffset, "error word offset");
+    if (!fs && pull_umma_eligible(a, d, tc_threshold)) {
+        pull_umma(a, d, accumulate, &hdr->pad[0], s);
+        return;
+    }
     if (!fs && pull_tma_eligible(a, d)) {
         pull_tma(a, d, tc_threshold, accumulate, &hdr->pad[0], s);
         return;

@@ -51,6 +51,10 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
 bool pull_tma_eligible(const PullTiles& a, const Dense& d);
 void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, uint32_t* err,
               cudaStream_t s);
+// tcgen05 pull kernel (pull_umma.cu): tc_threshold == 0 (every tile on the
+// TF32 tensor cores), F a multiple of 128, dense X.
+bool pull_umma_eligible(const PullTiles& a, const Dense& d, uint32_t tc_threshold);
+void pull_umma(const PullTiles& a, const Dense& d, int accumulate, uint32_t* err, cudaStream_t s);
 // Offset of the device error word inside a pull scratch.
 constexpr size_t kPullErrorOffset = 8;
 

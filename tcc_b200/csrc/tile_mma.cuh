@@ -66,7 +66,10 @@ __device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 
 // tile_mma with the column scale folded into B: B[k][n] = bit(n*8+k) ? c_k : 0,
 // x holds the unscaled rows (zeros for padding rows).  Lane (gid, tig) passes
 // c0 = scale of gather row tig, c1 = of row tig + 4.
-// pass2 == false: one TF32 pass, A and B rounded like cvt.rna.
+// pass2 == false: one TF32 pass on the raw fp32 bits -- the tensor core drops
+// the low 13 mantissa bits of each operand, the same arithmetic as the
+// tcgen05 kind::tf32 path -- with B split into its TF32 part and remainder
+// when `scaled`, so the column scale keeps fp32 accuracy.
 // pass2 == true: fp32-level split -- a = a_hi + a_lo, b = b_hi + b_lo (hi: low
 // 13 bits cleared, exact in TF32) and D += a_hi*b_hi + a_lo*b_hi (+ a_hi*b_lo
 // when `scaled`; with unit scales b_lo is 0).  The dropped a_lo*b_lo term is
@@ -79,14 +82,25 @@ __device__ __forceinline__ void tile_mma_scaled(float (&dacc)[4 * NP][4],
     const float bf0 = ((bm >> (gid * 8 + tig)) & 1ull) ? c0 : 0.f;
     const float bf1 = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? c1 : 0.f;
     if (!pass2) {
-        const uint32_t b[2] = {tf32_rna_bits(bf0), tf32_rna_bits(bf1)};
+        const uint32_t b[2] = {__float_as_uint(bf0), __float_as_uint(bf1)};
 #pragma unroll
         for (int p = 0; p < NP; ++p)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                const uint32_t a[4] = {tf32_rna_bits(comp(x[0][2 * p], c)), tf32_rna_bits(comp(x[0][2 * p + 1], c)),
-                                       tf32_rna_bits(comp(x[1][2 * p], c)), tf32_rna_bits(comp(x[1][2 * p + 1], c))};
+                const uint32_t a[4] = {__float_as_uint(comp(x[0][2 * p], c)), __float_as_uint(comp(x[0][2 * p + 1], c)),
+                                       __float_as_uint(comp(x[1][2 * p], c)), __float_as_uint(comp(x[1][2 * p + 1], c))};
                 mma_tf32_16x8x8(dacc[4 * p + c], a, b);
+            }
+        if (!scaled) return;
+        const uint32_t bl[2] = {__float_as_uint(bf0 - __uint_as_float(__float_as_uint(bf0) & 0xFFFFE000u)),
+                                __float_as_uint(bf1 - __uint_as_float(__float_as_uint(bf1) & 0xFFFFE000u))};
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t a[4] = {__float_as_uint(comp(x[0][2 * p], c)), __float_as_uint(comp(x[0][2 * p + 1], c)),
+                                       __float_as_uint(comp(x[1][2 * p], c)), __float_as_uint(comp(x[1][2 * p + 1], c))};
+                mma_tf32_16x8x8(dacc[4 * p + c], a, bl);
             }
         return;
     }

@@ -113,15 +113,20 @@ def test_swtcf_transposed(gpu, oracle, name, g, F):
     assert rel_fro(Z2.cpu().numpy(), oracle.csr_spmm_t(g, Gm)) <= TF32_TOL
 
 
-@pytest.fixture(params=["tma", "ldg"])
+PULL_KERNELS = ["default", "ldg", "tma", "umma"]
+
+
+@pytest.fixture(params=PULL_KERNELS)
 def pull_kernel(request, monkeypatch):
-    """Run a pull test on the register-gather kernel (default) and on the
-    bulk-copy gather kernel (TCC_PULL_KERNEL=tma); F that the bulk-copy kernel
-    does not take falls back to the register-gather kernel either way."""
-    if request.param == "tma":
-        monkeypatch.setenv("TCC_PULL_KERNEL", "tma")
-    else:
+    """Run a pull test on each pull kernel: the default dispatch, the
+    register-gather kernel (TCC_PULL_KERNEL=ldg), the bulk-copy gather kernel
+    (=tma) and the tcgen05 kernel (=umma; tc_threshold 0, F a multiple of
+    128).  Shapes a kernel does not take fall back to the register-gather
+    kernel."""
+    if request.param == "default":
         monkeypatch.delenv("TCC_PULL_KERNEL", raising=False)
+    else:
+        monkeypatch.setenv("TCC_PULL_KERNEL", request.param)
     return request.param
 
 
@@ -143,16 +148,23 @@ def test_bcsr_pull(gpu, oracle, pull_kernel, name, g, F, thr):
     assert rel_fro(Y2.cpu().numpy(), 2 * want) <= (FP32_TOL if thr > 64 else TF32_TOL)
 
 
-def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle, pull_kernel):
-    """TF32 on every tile (the cnic reference arithmetic) vs the oracle's tile
-    restatement of it, on both pull kernels; the TMA kernel's device error
-    word stays clear."""
+@pytest.mark.parametrize("kernel", ["ldg", "tma", "umma"])
+def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle, monkeypatch, kernel):
+    """TF32 on every tile (tc_threshold 0) against its exact restatement: the
+    register-gather kernel rounds X like cvt.rna (the oracle's tile
+    emulation); the bulk-copy and tcgen05 kernels hand the tensor core raw
+    fp32 bits and it drops the low 13 mantissa bits, i.e. A.trunc(X) summed
+    in fp32.  The device error word stays clear."""
+    monkeypatch.setenv("TCC_PULL_KERNEL", kernel)
     g = G.sbm(2000, 20, 120000, 40.0, 1.2, seed=12)
     rp, col = csr_dev(g)
     t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
     X = G.features(g.cols, 128, seed=9)
     Y = tiles.bcsr_spmm(t, dense(X), tc_threshold=0)
-    want = oracle.bcsr_spmm(oracle.bcsr_from_csr(g), X, tc_threshold=0)
+    if kernel == "ldg":
+        want = oracle.bcsr_spmm(oracle.bcsr_from_csr(g), X, tc_threshold=0)
+    else:
+        want = oracle.csr_spmm(g, oracle.tf32_trunc(X))
     assert rel_fro(Y.cpu().numpy(), want) <= FP32_TOL
     Y65 = tiles.bcsr_spmm(t, dense(X), tc_threshold=65)
     assert rel_fro(Y65.cpu().numpy(), oracle.csr_spmm(g, X)) <= FP32_TOL
