@@ -413,8 +413,11 @@ def main():
         import datetime
         import torch
         import torch.distributed as dist
+        from tcc_b200.partition import nccl_options
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                pg_options=nccl_options(),
+                                device_id=torch.device("cuda", local_rank))
         pg = True
     if args.profile:
         run_profile(args)

@@ -185,6 +185,26 @@ size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
  * whenever a call builds the plan (plan_ready = 0). */
 tcc_status tcc_pull_device_error(void* scratch, int* code, cudaStream_t stream);
 
+/* No counterpart in the reference.  The pull SpMM kernels run one persistent
+ * wave of blocks that fills every SM, so a kernel launched on another stream
+ * while they run (the NCCL kernels of the halo exchange) cannot become
+ * resident until they finish.  Pull kernels launched after
+ * tcc_set_grid_reserve(n) size their grids for all SMs but n, leaving room
+ * for such kernels; 0 restores full grids.  Process-wide setting. */
+void tcc_set_grid_reserve(uint32_t sms);
+uint32_t tcc_get_grid_reserve(void);
+
+/* No counterpart in the reference, whose multi-GPU path reads peer feature
+ * caches inside the SpMM kernel (cnic/src/core/spmm_kernel.cu:145-147).  Packs
+ * the rows a rank sends in the halo exchange of the row-partitioned SpMM:
+ * out[i, :F] = X[idx[i], :F] for i < n (int64 indices, F and both row
+ * strides multiples of 4, X and out 16-byte aligned).  An index outside
+ * [0, num_rows) writes a zero row and sets the device word *bad_flag (may be
+ * NULL). */
+tcc_status tcc_gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, const int64_t* idx,
+                           uint64_t n, float* out, uint64_t ldo, uint32_t F, uint32_t* bad_flag,
+                           cudaStream_t stream);
+
 /* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
  * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):
  * C[num_rows x F] = diag(rs) * A * diag(cs) * B[num_cols x F]; row windows own

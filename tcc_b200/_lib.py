@@ -88,6 +88,9 @@ PROTOTYPES = {
     "tcc_tiles_fill_bcsc": (_st, [_vp, C.POINTER(Bcsc), _vp]),
     "tcc_pull_scratch_bytes": (C.c_size_t, [_u32, _u32]),
     "tcc_pull_device_error": (_st, [_vp, C.POINTER(_i), _vp]),
+    "tcc_set_grid_reserve": (None, [_u32]),
+    "tcc_get_grid_reserve": (_u32, []),
+    "tcc_gather_rows": (_st, [_vp, _u64, _u64, _vp, _u64, _vp, _u64, _u32, _vp, _vp]),
     "tcc_bcsr_spmm": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i, _vp,
                             C.c_size_t, _i, _vp]),
     "tcc_bcsr_spmm_noalloc": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,

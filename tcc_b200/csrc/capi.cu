@@ -379,6 +379,18 @@ size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
     return tcc::pull_scratch_bytes(num_windows, num_tiles);
 }
 
+void tcc_set_grid_reserve(uint32_t sms) { tcc::set_grid_reserve(sms); }
+uint32_t tcc_get_grid_reserve(void) { return tcc::grid_reserve(); }
+
+tcc_status tcc_gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, const int64_t* idx,
+                           uint64_t n, float* out, uint64_t ldo, uint32_t F, uint32_t* bad_flag,
+                           cudaStream_t stream) {
+    return guarded("tcc_gather_rows", [&] {
+        TCC_REQUIRE(n == 0 || (X && idx && out), "X, idx and out must not be NULL");
+        tcc::gather_rows(X, ldx, num_rows, idx, n, out, ldo, F, bad_flag, stream);
+    });
+}
+
 tcc_status tcc_pull_device_error(void* scratch, int* code, cudaStream_t stream) {
     return guarded("tcc_pull_device_error", [&] {
         TCC_REQUIRE(scratch && code, "scratch and code must not be NULL");

@@ -44,6 +44,11 @@ struct Error : std::runtime_error {
 inline unsigned ceil_div(uint64_t a, uint64_t b) { return (unsigned)((a + b - 1) / b); }
 
 int sm_count();
+// SMs the pull kernels size their grids for: all minus the reserve set by
+// tcc_set_grid_reserve (room for kernels on other streams to become resident).
+int grid_sms();
+void set_grid_reserve(uint32_t sms);
+uint32_t grid_reserve();
 
 // ------------------------------------------------------------ device side --
 

@@ -435,7 +435,7 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
               cudaStream_t s) {
     const uint32_t bw = d.F <= kMaxBox ? d.F : kMaxBox;
     const uint32_t slices = d.F <= kMaxBox ? 1 : d.F / kMaxBox;
-    const uint32_t ctas = (uint32_t)sm_count();
+    const uint32_t ctas = (uint32_t)grid_sms();
     const uint32_t G = ctas * kTW;
     if (!accumulate && a.num_tiles > 0)
         zero_reduced_kernel<<<std::min<unsigned>(ceil_div(a.num_windows, 8), ctas * 8), 256, 0, s>>>(

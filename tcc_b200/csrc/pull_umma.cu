@@ -577,7 +577,7 @@ void pull_umma(const PullTiles& a, const Dense& d, int accumulate, uint32_t* err
                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(TCC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the X rows");
-    const uint32_t ctas = (uint32_t)sm_count();
+    const uint32_t ctas = (uint32_t)grid_sms();
     if (!accumulate && a.num_tiles > 0)
         zero_reduced_umma<<<std::min<unsigned>(ceil_div(a.num_windows, 8), ctas * 8), 256, 0, s>>>(
             a.win_offset, a.num_windows, a.num_tiles, ctas, d.Y, d.ldy, d.F, a.num_out);

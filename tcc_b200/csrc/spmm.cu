@@ -21,6 +21,8 @@
 #include "primitives.cuh"
 #include "tile_mma.cuh"
 
+#include <algorithm>
+#include <atomic>
 #include <cstddef>
 #include <mutex>
 
@@ -35,6 +37,19 @@ int sm_count() {
     std::lock_guard<std::mutex> lock(mu);
     if (!cache[dev]) TCC_CUDA(cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev));
     return cache[dev];
+}
+
+namespace {
+std::atomic<uint32_t> g_grid_reserve{0};
+}  // namespace
+
+void set_grid_reserve(uint32_t sms) { g_grid_reserve.store(sms); }
+uint32_t grid_reserve() { return g_grid_reserve.load(); }
+
+int grid_sms() {
+    const int n = sm_count();
+    const int r = (int)std::min<uint32_t>(g_grid_reserve.load(), (uint32_t)std::max(0, n - 1));
+    return n - r;
 }
 
 namespace {
@@ -448,7 +463,7 @@ void launch_pull(const PullTiles& a, const Dense& d, const uint4* desc, PlanHead
     int per_sm = 0;
     TCC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kPullWarps * 32, smem));
     const uint64_t want = (max_chunks + kPullWarps - 1) / kPullWarps;
-    const uint64_t resident = (uint64_t)std::max(1, per_sm) * sm_count();
+    const uint64_t resident = (uint64_t)std::max(1, per_sm) * grid_sms();
     const unsigned gx = (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(want, resident));
     const unsigned gy = ceil_div(d.F, 64 * NP);
     k<<<dim3(gx, gy), kPullWarps * 32, smem, s>>>(a, d, desc, hdr, thr, accumulate, fs);

@@ -7,13 +7,18 @@ of remote columns; the halo is compacted to the distinct remote columns, and
 each owner learns once, at set-up, which of its rows every peer needs.
 
 One SpMM step on rank g:
-  1. pack the rows peers need (index_select) and start an NCCL all-to-all
-     (uneven splits, one message per peer pair) on NCCL's stream;
-  2. meanwhile run the local-column tiles: Y = A_loc · X[P_g];
+  1. on a high-priority side stream, pack the rows peers need (the
+     tcc_gather_rows kernel) and start an NCCL all-to-all (uneven splits, one
+     message per peer pair);
+  2. meanwhile run the local-column tiles on the caller's stream:
+     Y = A_loc · X[P_g];
   3. wait for the halo, then Y += A_halo · X_halo.
 A_loc and A_halo are BCSR tilings of the local rows with column ids remapped to
-[0, |P_g|) and [0, |halo|).  The same class runs on CPU/gloo ranks without
-tilings, for testing the index plumbing.
+[0, |P_g|) and [0, |halo|).  The process group should give NCCL high-priority
+streams (ProcessGroupNCCL.Options.is_high_priority_stream) so the exchange's
+kernels are scheduled ahead of the local tiles' queued blocks.  The same class
+runs on CPU tensors over gloo without tilings, as the test harness of the
+index plumbing (packing with index_select there).
 
 This replaces the reference's multi-GPU feature access -- direct loads from a
 peer GPU's feature cache inside the kernel
@@ -24,6 +29,27 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+
+
+def gather_rows(X: torch.Tensor, idx: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+    """out[i] = X[idx[i]] on the GPU (tcc_gather_rows); idx int64."""
+    import ctypes as C
+    from . import _lib as L
+    assert X.is_cuda and X.dtype == torch.float32 and out.dtype == torch.float32
+    assert idx.dtype == torch.int64 and out.shape[0] == idx.numel() and out.shape[1] == X.shape[1]
+    s = (stream or torch.cuda.current_stream(X.device)).cuda_stream
+    L.call("tcc_gather_rows", C.c_void_p(X.data_ptr()), X.stride(0), X.shape[0],
+           C.c_void_p(idx.data_ptr()), idx.numel(), C.c_void_p(out.data_ptr()), out.stride(0),
+           X.shape[1], None, C.c_void_p(s))
+    return out
+
+
+def nccl_options():
+    """ProcessGroupNCCL options with high-priority NCCL streams (the halo
+    exchange then overlaps the local tiles instead of queueing behind them)."""
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    return opts
 
 
 def balanced_bounds(degrees: torch.Tensor, parts: int) -> list:
@@ -89,6 +115,9 @@ class DistGraph:
         self.cs_local = None if cs_global is None else cs_global[r0:r1].contiguous()
         self.cs_halo = None if cs_global is None else cs_global[self.halo].contiguous()
         self.tc_threshold = tc_threshold
+        self._bufs = {}
+        self._side = None
+        self.comm_sms = 32  # SMs left to the exchange during the local tiles (measured best of 0-32)
         self.tiles_loc = self.tiles_halo = None
         if build_tiles:
             from . import tiles
@@ -110,25 +139,55 @@ class DistGraph:
     def halo_rows(self) -> int:
         return int(self.halo.numel())
 
+    def _buf(self, name, rows, like):
+        key = (name, like.shape[1], like.dtype, like.device)
+        b = self._bufs.get(key)
+        if b is None or b.shape[0] != rows:
+            b = torch.empty((rows, like.shape[1]), dtype=like.dtype, device=like.device)
+            self._bufs[key] = b
+        return b
+
     def exchange(self, X_local: torch.Tensor, async_op: bool = True):
-        """Start the halo exchange; returns (halo buffer, work handle or None)."""
-        F = X_local.shape[1]
-        recv = torch.empty((self.halo_rows, F), dtype=X_local.dtype, device=X_local.device)
+        """Start the halo exchange; returns (halo buffer, work handle or None).
+        The halo buffer is reused by the next exchange of the same width."""
+        recv = self._buf("recv", self.halo_rows, X_local)
         if self.world == 1:
             return recv, None
-        send = X_local.index_select(0, self.send_idx)
-        work = dist.all_to_all_single(recv, send, self.recv_counts, self.send_counts,
-                                      group=self.group, async_op=async_op)
+        send = self._buf("send", self.send_idx.numel(), X_local)
+        if not X_local.is_cuda:
+            torch.index_select(X_local, 0, self.send_idx, out=send)
+            work = dist.all_to_all_single(recv, send, self.recv_counts, self.send_counts,
+                                          group=self.group, async_op=async_op)
+            return recv, work
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=X_local.device, priority=-1)
+        side = self._side
+        side.wait_stream(torch.cuda.current_stream(X_local.device))
+        with torch.cuda.stream(side):
+            gather_rows(X_local, self.send_idx, send, stream=side)
+            work = dist.all_to_all_single(recv, send, self.recv_counts, self.send_counts,
+                                          group=self.group, async_op=True)
+        if not async_op:
+            work.wait()
+            work = None
         return recv, work
 
     def spmm(self, X_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """Y[P_g] = (diag(rs) A diag(cs) X)[P_g], exchange overlapped with the
         local-column tiles."""
         from . import tiles
+        from . import _lib as L
         X_local = X_local.contiguous()
         halo, work = self.exchange(X_local)
-        Y = tiles.bcsr_spmm(self.tiles_loc, X_local, out, tc_threshold=self.tc_threshold,
-                            rs=self.rs, cs=self.cs_local)
+        # leave SMs for the exchange's NCCL kernels while the local tiles run
+        reserve = self.comm_sms if work is not None else 0
+        prev = L.lib().tcc_get_grid_reserve()
+        L.lib().tcc_set_grid_reserve(reserve)
+        try:
+            Y = tiles.bcsr_spmm(self.tiles_loc, X_local, out, tc_threshold=self.tc_threshold,
+                                rs=self.rs, cs=self.cs_local)
+        finally:
+            L.lib().tcc_set_grid_reserve(prev)
         if work is not None:
             work.wait()
         if self.tiles_halo is not None:

@@ -27,8 +27,10 @@ def _worker(rank, world, port, q):
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
+    from tcc_b200.partition import nccl_options
     dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=120))
+                            timeout=datetime.timedelta(seconds=120), pg_options=nccl_options(),
+                            device_id=torch.device("cuda", rank))
     try:
         from tcc_b200 import graphs as G
         from tcc_b200 import tiles
