@@ -50,6 +50,11 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--tc-threshold", type=int, default=12)
     p.add_argument("--scale", type=int, default=20, help="R-MAT scale (20 = config 2)")
+    p.add_argument("--workload", choices=["spmm", "gcn4"], default="spmm",
+                   help="spmm: the config-2 SpMM step (headline); gcn4: config-4 GCN epoch time "
+                        "(tcc_b200.train_gcn, epochs = --steps)")
+    p.add_argument("--transform-first", action="store_true",
+                   help="gcn4: compute layer 2 as A.(H.W) instead of (A.H).W")
     p.add_argument("--profile", choices=["fwd", "bwd"], default=None,
                    help="build the workload, run only the forward (or transposed) pull "
                         "--steps times and exit: the command ncu captures")
@@ -408,6 +413,16 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus and rank == 0:
         print(f"note: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if args.workload == "gcn4":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference GCN trainer needs DGL "
+                                  "and its absent ipc_service sampler"}), flush=True)
+            return
+        from tcc_b200 import train_gcn
+        train_gcn.main(["--epochs", str(max(args.steps, 2))] +
+                       (["--transform-first"] if args.transform_first else []))
+        return
     pg = False
     if world > 1 and args.impl == "ours":
         import datetime

@@ -223,26 +223,30 @@ def config(idx: int, shrink: int = 0):
 # --------------------------------------------------- GPU (torch) generator --
 
 def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
-             abcd=(0.57, 0.19, 0.19, 0.05), chunk: int = 1 << 26):
+             abcd=(0.57, 0.19, 0.19, 0.05), chunk: int = 1 << 26, n: int | None = None):
     """R-MAT on the GPU with torch's seeded generator: ``edges`` directed edges on
     2**scale nodes, symmetrised, deduplicated, self-loops added.
 
-    Every caller with the same (scale, edges, seed) draws the same edges, so each
-    rank of a multi-GPU job can build just its rows: ``row_range = (r0, r1)``
-    keeps rows r0 <= r < r1.  Returns (rowptr int64 [r1-r0+1], col int32 [nnz]
-    global column ids, degrees int64 [2**scale] of the symmetrised multigraph
-    before deduplication + 1 self-loop, used for balancing partitions).
+    With ``n`` < 2**scale nodes, edges touching a node >= n are dropped and more
+    are drawn until ``edges`` directed edges (before removing self-edges) remain
+    (config 4's 2,449,029 nodes).  Every caller with the same arguments draws
+    the same edges, so each rank of a multi-GPU job can build just its rows:
+    ``row_range = (r0, r1)`` keeps rows r0 <= r < r1.  Returns (rowptr int64
+    [r1-r0+1], col int32 [nnz] global column ids, degrees int64 [n] of the
+    symmetrised multigraph before deduplication + 1 self-loop, used for
+    balancing partitions).
     """
     import torch
-    n = 1 << scale
+    n = (1 << scale) if n is None else n
     r0, r1 = (0, n) if row_range is None else row_range
     a, b, c, _ = abcd
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     keys = []
     deg = torch.ones(n, dtype=torch.int64, device=device)  # self-loop
-    for start in range(0, edges, chunk):
-        k = min(chunk, edges - start)
+    have = 0
+    while have < edges:
+        k = min(chunk, edges - have) if n == 1 << scale else chunk
         u = torch.zeros(k, dtype=torch.int64, device=device)
         v = torch.zeros(k, dtype=torch.int64, device=device)
         for level in range(scale):
@@ -250,6 +254,12 @@ def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
             bit = 1 << (scale - 1 - level)
             u += (r >= a + b).to(torch.int64) * bit
             v += (((r >= a) & (r < a + b)) | (r >= a + b + c)).to(torch.int64) * bit
+        if n != 1 << scale:
+            inside = (u < n) & (v < n)
+            u, v = u[inside], v[inside]
+            take = min(u.numel(), edges - have)
+            u, v = u[:take], v[:take]
+        have += u.numel()
         keep = u != v
         u, v = u[keep], v[keep]
         deg += torch.bincount(u, minlength=n) + torch.bincount(v, minlength=n)
