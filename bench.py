@@ -50,11 +50,16 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--tc-threshold", type=int, default=12)
     p.add_argument("--scale", type=int, default=20, help="R-MAT scale (20 = config 2)")
-    p.add_argument("--workload", choices=["spmm", "gcn4"], default="spmm",
-                   help="spmm: the config-2 SpMM step (headline); gcn4: config-4 GCN epoch time "
-                        "(tcc_b200.train_gcn, epochs = --steps)")
+    p.add_argument("--workload", choices=["spmm", "gcn4", "config5"], default="spmm",
+                   help="spmm: the config-2 SpMM step (headline, weak scaling); gcn4: config-4 GCN "
+                        "epoch time (tcc_b200.train_gcn, epochs = --steps); config5: the scale-26 "
+                        "forward SpMM, strong scaling")
     p.add_argument("--transform-first", action="store_true",
                    help="gcn4: compute layer 2 as A.(H.W) instead of (A.H).W")
+    p.add_argument("--scale5", type=int, default=26, help="config5: R-MAT scale (26 = config 5)")
+    p.add_argument("--c5-mode", choices=["exchange", "replicated"], default="exchange",
+                   help="config5 on N > 1 GPUs: exchange the X halo every step, or all-gather X "
+                        "once at set-up (static input features) and run without communication")
     p.add_argument("--profile", choices=["fwd", "bwd"], default=None,
                    help="build the workload, run only the forward (or transposed) pull "
                         "--steps times and exit: the command ncu captures")
@@ -301,7 +306,9 @@ def run_ours(args, rank, world, local_rank):
     n_loc = dg.n_local
     b_alg = 4 * F * (n_loc + n_loc) + 8 * dg.nnz + 4 * (n_loc + 1)
     achieved = b_alg / (fwd_ms * 1e-3) / 1e9
-    per_step_launches = 2 * (2 if dg.tiles_halo is None else 4)
+    # per SpMM: pull + zero pass on the local tiles; with a halo also the pack
+    # kernel and pull + zero pass on the halo tiles
+    per_step_launches = 2 * (2 if dg.tiles_halo is None else 5)
     line = {
         "metric": "SpMM GFLOP/s (2*nnz*F)",
         "value": round(flops_step / (ms_per_step * 1e-3) / 1e9, 2),
@@ -341,6 +348,131 @@ def run_ours(args, rank, world, local_rank):
         g = host_csr(W["rowptr"], W["col"], W["n"])
         s = W["s"].cpu().numpy()
         line["cpu_baseline"] = cpu_baseline(g, X.cpu().numpy(), s, s)
+    print(json.dumps(line), flush=True)
+
+
+def run_config5(args, rank, world, local_rank):
+    """Config 5: one directed R-MAT graph (scale --scale5, 16 edges per node,
+    seed 4, deduplicated, row-normalised), forward Y = A.X with F = 128 on 1..N
+    GPUs -- strong scaling: every N partitions the same graph by rows."""
+    import torch
+    import torch.distributed as dist
+    from tcc_b200 import graphs as G
+    from tcc_b200.partition import DistGraph, balanced_bounds
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    scale = args.scale5
+    edges = 16 << scale
+    t0 = time.time()
+    deg = G.rmat_gpu_degrees(scale, edges, seed=4, device=device, symmetric=False, loops=False)
+    bounds = balanced_bounds(deg, world)
+    del deg
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    lrp, lcol, _ = G.rmat_gpu(scale, edges, seed=4, device=device, row_range=(r0, r1),
+                              symmetric=False, loops=False)
+    d = torch.diff(lrp)
+    rs = torch.where(d > 0, 1.0 / d.clamp(min=1).to(torch.float64),
+                     torch.zeros_like(d, dtype=torch.float64)).to(torch.float32)
+    torch.cuda.synchronize()
+    gen_s = time.time() - t0
+    t0 = time.time()
+    F = 128
+    n = 1 << scale
+    replicated = args.c5_mode == "replicated" and world > 1
+    allgather_s = None
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4000 + rank)
+    X = torch.randn((r1 - r0, F), generator=gen, device=device)
+    Y = torch.empty_like(X)
+    if replicated:
+        # X is static input: all-gather the row blocks once, then every step
+        # runs the rank's rows against the full local copy (no exchange)
+        from tcc_b200 import tiles as T
+        tl = T.from_csr(lrp, lcol, r1 - r0, n, kind="bcsr")
+        del lcol
+        torch.cuda.empty_cache()
+        torch.cuda.synchronize()
+        conv_s = time.time() - t0
+        Xfull = torch.empty((n, F), device=device)
+        parts = [Xfull[bounds[g]:bounds[g + 1]] for g in range(world)]
+        dist.barrier()
+        t1 = time.time()
+        dist.all_gather(parts, X)
+        torch.cuda.synchronize()
+        allgather_s = time.time() - t1
+
+        import types
+        dg = types.SimpleNamespace(nnz=tl.nnz, halo_rows=0)
+
+        def spmm():
+            T.bcsr_spmm(tl, Xfull, Y, tc_threshold=args.tc_threshold, rs=rs)
+    else:
+        dg = DistGraph(lrp, lcol, bounds, rs_local=rs, cs_global=None, tc_threshold=args.tc_threshold)
+        del lcol
+        torch.cuda.empty_cache()
+        torch.cuda.synchronize()
+        conv_s = time.time() - t0
+
+        def spmm():
+            dg.spmm(X, Y)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        spmm()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        spmm()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device)
+    tot = torch.tensor([float(dg.nnz), float(dg.halo_rows)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms = t.item()
+    nnz_total, halo_total = tot.tolist()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    b_alg = 4 * F * (n + n) + 8 * nnz_total + 4 * (n + 1)  # the whole job's SpMM
+    achieved = b_alg / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "SpMM GFLOP/s (2*nnz*F)",
+        "value": round(2.0 * nnz_total * F / (ms * 1e-3) / 1e9, 2),
+        "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded directed R-MAT, torch GPU generator seed 4)",
+        "config": {"workload": "config5: R-MAT 2^%d nodes, %d directed edges (16 per node), "
+                               "deduplicated, row-normalised, F=128, forward A.X" % (scale, edges),
+                   "rmat_scale": scale, "nnz_total": int(nnz_total), "nnz_rank0": dg.nnz,
+                   "halo_rows_total": int(halo_total), "tc_threshold": args.tc_threshold,
+                   "parallelism": (f"{world}-way 1D row partition, " +
+                                   ("X all-gathered once at set-up (static input features)"
+                                    if replicated else "halo exchanged every step"))
+                   if world > 1 else "1 GPU",
+                   "allgather_s": None if allgather_s is None else round(allgather_s, 3),
+                   "gen_s": round(gen_s, 2), "convert_s": round(conv_s, 2)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved / world, 1), "peak": peak,
+                     "unit": "GB/s per GPU", "frac": round(achieved / world / peak, 4),
+                     "traffic": None, "kernel": "forward SpMM (exchange + local + halo tiles)",
+                     "peak_kind": peak_kind},
+        "e2e": None,
+        "gpu_launches": args.steps * (2 if world == 1 or replicated else 5),
+        "clocks": clocks,
+    }
     print(json.dumps(line), flush=True)
 
 
@@ -438,7 +570,13 @@ def main():
         run_profile(args)
         return
     try:
-        if args.impl == "ours":
+        if args.impl == "ours" and args.workload == "config5":
+            run_config5(args, rank, world, local_rank)
+        elif args.impl == "reference" and args.workload == "config5":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no "
+                                  "row-partitioned multi-GPU SpMM"}), flush=True)
+        elif args.impl == "ours":
             run_ours(args, rank, world, local_rank)
         else:
             run_reference(args, rank, world, local_rank)

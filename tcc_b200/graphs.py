@@ -222,28 +222,12 @@ def config(idx: int, shrink: int = 0):
 
 # --------------------------------------------------- GPU (torch) generator --
 
-def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
-             abcd=(0.57, 0.19, 0.19, 0.05), chunk: int = 1 << 26, n: int | None = None):
-    """R-MAT on the GPU with torch's seeded generator: ``edges`` directed edges on
-    2**scale nodes, symmetrised, deduplicated, self-loops added.
-
-    With ``n`` < 2**scale nodes, edges touching a node >= n are dropped and more
-    are drawn until ``edges`` directed edges (before removing self-edges) remain
-    (config 4's 2,449,029 nodes).  Every caller with the same arguments draws
-    the same edges, so each rank of a multi-GPU job can build just its rows:
-    ``row_range = (r0, r1)`` keeps rows r0 <= r < r1.  Returns (rowptr int64
-    [r1-r0+1], col int32 [nnz] global column ids, degrees int64 [n] of the
-    symmetrised multigraph before deduplication + 1 self-loop, used for
-    balancing partitions).
-    """
+def _rmat_gpu_edges(scale, edges, seed, device, abcd, chunk, n):
+    """Yields the (u, v) int64 edge chunks of rmat_gpu (self-edges removed)."""
     import torch
-    n = (1 << scale) if n is None else n
-    r0, r1 = (0, n) if row_range is None else row_range
     a, b, c, _ = abcd
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
-    keys = []
-    deg = torch.ones(n, dtype=torch.int64, device=device)  # self-loop
     have = 0
     while have < edges:
         k = min(chunk, edges - have) if n == 1 << scale else chunk
@@ -261,13 +245,55 @@ def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
             u, v = u[:take], v[:take]
         have += u.numel()
         keep = u != v
-        u, v = u[keep], v[keep]
-        deg += torch.bincount(u, minlength=n) + torch.bincount(v, minlength=n)
-        for x, y in ((u, v), (v, u)):
+        yield u[keep], v[keep]
+
+
+def rmat_gpu_degrees(scale: int, edges: int, seed: int, device, abcd=(0.57, 0.19, 0.19, 0.05),
+                     chunk: int = 1 << 26, n: int | None = None, symmetric: bool = True,
+                     loops: bool = True):
+    """Row nonzero counts of rmat_gpu's matrix before deduplication, without
+    materialising it (partition bounds for a job whose ranks build only their
+    rows)."""
+    import torch
+    n = (1 << scale) if n is None else n
+    deg = torch.full((n,), 1 if loops else 0, dtype=torch.int64, device=device)
+    for u, v in _rmat_gpu_edges(scale, edges, seed, device, abcd, chunk, n):
+        deg += torch.bincount(u, minlength=n)
+        if symmetric:
+            deg += torch.bincount(v, minlength=n)
+    return deg
+
+
+def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
+             abcd=(0.57, 0.19, 0.19, 0.05), chunk: int = 1 << 26, n: int | None = None,
+             symmetric: bool = True, loops: bool = True):
+    """R-MAT on the GPU with torch's seeded generator: ``edges`` directed edges on
+    2**scale nodes, symmetrised (unless ``symmetric`` is False), deduplicated,
+    self-loops added (unless ``loops`` is False).
+
+    With ``n`` < 2**scale nodes, edges touching a node >= n are dropped and more
+    are drawn until ``edges`` directed edges (before removing self-edges) remain
+    (config 4's 2,449,029 nodes).  Every caller with the same arguments draws
+    the same edges, so each rank of a multi-GPU job can build just its rows:
+    ``row_range = (r0, r1)`` keeps rows r0 <= r < r1.  Returns (rowptr int64
+    [r1-r0+1], col int32 [nnz] global column ids, degrees int64 [n]: row
+    nonzero counts before deduplication, used for balancing partitions).
+    """
+    import torch
+    n = (1 << scale) if n is None else n
+    r0, r1 = (0, n) if row_range is None else row_range
+    keys = []
+    deg = torch.full((n,), 1 if loops else 0, dtype=torch.int64, device=device)
+    for u, v in _rmat_gpu_edges(scale, edges, seed, device, abcd, chunk, n):
+        deg += torch.bincount(u, minlength=n)
+        if symmetric:
+            deg += torch.bincount(v, minlength=n)
+        for x, y in (((u, v), (v, u)) if symmetric else ((u, v),)):
             m = (x >= r0) & (x < r1)
             keys.append(((x[m] - r0) << 32) | y[m])
-    loops = torch.arange(r0, r1, dtype=torch.int64, device=device)
-    keys.append(((loops - r0) << 32) | loops)
+    if loops:
+        diag = torch.arange(r0, r1, dtype=torch.int64, device=device)
+        keys.append(((diag - r0) << 32) | diag)
     keys = torch.unique(torch.cat(keys))  # sorted, deduplicated
     rows = (keys >> 32)
     col = (keys & 0xFFFFFFFF).to(torch.int32)

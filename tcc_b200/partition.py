@@ -88,32 +88,42 @@ class DistGraph:
         self.n_local = r1 - r0
         dev = rowptr.device
         self.device = dev
-        col64 = col.to(torch.int64)
-        nnz = col64.numel()
-        self.nnz = nnz
-        rows = torch.repeat_interleave(torch.arange(self.n_local, device=dev),
-                                       torch.diff(rowptr))
-        is_loc = (col64 >= r0) & (col64 < r1)
-        # compacted halo: distinct remote columns, ascending (so grouped by owner)
-        self.halo = torch.unique(col64[~is_loc])
-        bnd = torch.tensor(self.bounds, dtype=torch.int64, device=dev)
-        owner = torch.searchsorted(bnd, self.halo, right=True) - 1
-        self.recv_counts = torch.bincount(owner, minlength=self.world).tolist()
-        # tell every owner which of its rows we need (local ids at the owner)
-        req_local = (self.halo - bnd[owner]).to(torch.int64)
-        self.send_counts = self._exchange_counts(self.recv_counts)
-        self.send_idx = torch.empty(sum(self.send_counts), dtype=torch.int64, device=dev)
-        if self.world > 1:
+        self.nnz = col.numel()
+        if self.world == 1:
+            # every column is local: the CSR is the local-column CSR as is
+            self.halo = torch.empty(0, dtype=torch.int64, device=dev)
+            self.recv_counts = [0]
+            self.send_counts = [0]
+            self.send_idx = torch.empty(0, dtype=torch.int64, device=dev)
+            self.loc_rowptr, self.loc_col = rowptr, col.to(torch.int32)
+            self.halo_rowptr = torch.zeros(self.n_local + 1, dtype=torch.int64, device=dev)
+            self.halo_col = torch.empty(0, dtype=torch.int32, device=dev)
+        else:
+            col64 = col.to(torch.int64)
+            rows = torch.repeat_interleave(torch.arange(self.n_local, device=dev),
+                                           torch.diff(rowptr))
+            is_loc = (col64 >= r0) & (col64 < r1)
+            # compacted halo: distinct remote columns, ascending (so grouped by owner)
+            self.halo = torch.unique(col64[~is_loc])
+            bnd = torch.tensor(self.bounds, dtype=torch.int64, device=dev)
+            owner = torch.searchsorted(bnd, self.halo, right=True) - 1
+            self.recv_counts = torch.bincount(owner, minlength=self.world).tolist()
+            # tell every owner which of its rows we need (local ids at the owner)
+            req_local = (self.halo - bnd[owner]).to(torch.int64)
+            self.send_counts = self._exchange_counts(self.recv_counts)
+            self.send_idx = torch.empty(sum(self.send_counts), dtype=torch.int64, device=dev)
             dist.all_to_all_single(self.send_idx, req_local, self.send_counts, self.recv_counts,
                                    group=group)
-        # local-column and halo-column CSRs of the local rows, remapped ids
-        self.loc_rowptr, self.loc_col = _csr_from_pairs(rows[is_loc], col64[is_loc] - r0,
-                                                        self.n_local)
-        hcol = torch.searchsorted(self.halo, col64[~is_loc])
-        self.halo_rowptr, self.halo_col = _csr_from_pairs(rows[~is_loc], hcol, self.n_local)
+            # local-column and halo-column CSRs of the local rows, remapped ids
+            self.loc_rowptr, self.loc_col = _csr_from_pairs(rows[is_loc], col64[is_loc] - r0,
+                                                            self.n_local)
+            hcol = torch.searchsorted(self.halo, col64[~is_loc])
+            self.halo_rowptr, self.halo_col = _csr_from_pairs(rows[~is_loc], hcol, self.n_local)
+            del rows, col64, is_loc, hcol
         self.rs = rs_local
         self.cs_local = None if cs_global is None else cs_global[r0:r1].contiguous()
-        self.cs_halo = None if cs_global is None else cs_global[self.halo].contiguous()
+        self.cs_halo = None if cs_global is None or not self.halo.numel() else \
+            cs_global[self.halo].contiguous()
         self.tc_threshold = tc_threshold
         self._bufs = {}
         self._side = None
