@@ -50,6 +50,11 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--tc-threshold", type=int, default=12)
     p.add_argument("--scale", type=int, default=20, help="R-MAT scale (20 = config 2)")
+    p.add_argument("--dist-mode", choices=["replicated", "exchange"], default="replicated",
+                   help="spmm on N > 1 GPUs: 'replicated' = the config-2 job split by rows "
+                        "(strong scaling; X and G resident on every GPU, all-gathered from the "
+                        "ranks' row blocks in the e2e leg); 'exchange' = config 2 per GPU "
+                        "(weak scaling, scale 20 + log2 N) with the X halo exchanged every step")
     p.add_argument("--workload", choices=["spmm", "gcn4", "config5"], default="spmm",
                    help="spmm: the config-2 SpMM step (headline, weak scaling); gcn4: config-4 GCN "
                         "epoch time (tcc_b200.train_gcn, epochs = --steps); config5: the scale-26 "
@@ -176,6 +181,39 @@ def build_workload(scale, device, world=1, rank=0, tc_threshold=12):
                 gen_s=gen_s, conv_s=conv_s, full_rowptr=rowptr, full_col=col)
 
 
+def build_replicated(scale, device, world=1, rank=0, tc_threshold=12):
+    """Config 2 split by rows for strong scaling: every rank generates the whole
+    graph (same seeds), keeps its nnz-balanced row block tiled against the
+    global columns, and holds full copies of X and G (the same seeded draws on
+    every rank, i.e. what an all-gather of the row blocks produces)."""
+    import torch
+    from tcc_b200 import graphs as G
+    from tcc_b200 import tiles as T
+    from tcc_b200.partition import balanced_bounds
+    t0 = time.time()
+    rowptr, col, _ = G.rmat_gpu(scale, 16 << scale, seed=1, device=device)
+    deg = torch.diff(rowptr)
+    n = deg.numel()
+    s = torch.where(deg > 0, deg.to(torch.float64).clamp(min=1).rsqrt(),
+                    torch.zeros_like(deg, dtype=torch.float64)).to(torch.float32)
+    bounds = balanced_bounds(deg, world)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    lrp = (rowptr[r0:r1 + 1] - rowptr[r0]).contiguous()
+    lcol = col[rowptr[r0]:rowptr[r1]].contiguous()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000)
+    X = torch.randn((n, 128), generator=gen, device=device)
+    Gm = torch.randn((n, 128), generator=gen, device=device)
+    torch.cuda.synchronize()
+    gen_s = time.time() - t0
+    t0 = time.time()
+    tl = T.from_csr(lrp, lcol, r1 - r0, n, kind="bcsr")
+    torch.cuda.synchronize()
+    conv_s = time.time() - t0
+    return dict(tiles=tl, n=n, bounds=bounds, r0=r0, r1=r1, rowptr=lrp, col=lcol, s=s,
+                rs=s[r0:r1].contiguous(), X=X, G=Gm, gen_s=gen_s, conv_s=conv_s)
+
+
 def host_csr(rowptr, col, cols):
     """The device CSR as the oracle's host Csr (uint64 rowptr, uint32 col)."""
     from tcc_b200 import graphs as G
@@ -217,22 +255,44 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    scale = args.scale + int(round(math.log2(world)))
-    W = build_workload(scale, device, world, rank, args.tc_threshold)
-    dg = W["dg"]
+    replicated = args.dist_mode == "replicated" or world == 1
+    scale = args.scale if replicated else args.scale + int(round(math.log2(world)))
     F = 128
-    X, Gm = W["X"], W["G"]
-    Y = torch.empty_like(X)
-    Z = torch.empty_like(Gm)
     stream = torch.cuda.current_stream()
+    if replicated:
+        W = build_replicated(scale, device, world, rank, args.tc_threshold)
+        tl, rs_loc, s_all = W["tiles"], W["rs"], W["s"]
+        X, Gm = W["X"], W["G"]  # full copies on every GPU
+        r0, r1 = W["r0"], W["r1"]
+        Y = torch.empty((r1 - r0, F), device=device)
+        Z = torch.empty_like(Y)
+        from tcc_b200 import tiles as T
 
-    def step(fwd_events=None):
-        if fwd_events:
-            fwd_events[0].record(stream)
-        dg.spmm(X, Y)
-        if fwd_events:
-            fwd_events[1].record(stream)
-        dg.spmm_t(Gm, Z)  # A^T G: A is symmetric, same partition and tiles
+        def step(fwd_events=None):
+            if fwd_events:
+                fwd_events[0].record(stream)
+            T.bcsr_spmm(tl, X, Y, tc_threshold=args.tc_threshold, rs=rs_loc, cs=s_all)
+            if fwd_events:
+                fwd_events[1].record(stream)
+            # A^T G: A is symmetric, so the rank's rows of A^T are its rows of A
+            T.bcsr_spmm(tl, Gm, Z, tc_threshold=args.tc_threshold, rs=rs_loc, cs=s_all)
+
+        import types
+        dg = types.SimpleNamespace(nnz=tl.nnz, halo_rows=0, n_local=r1 - r0, tiles_halo=None)
+    else:
+        W = build_workload(scale, device, world, rank, args.tc_threshold)
+        dg = W["dg"]
+        X, Gm = W["X"], W["G"]
+        Y = torch.empty_like(X)
+        Z = torch.empty_like(Gm)
+
+        def step(fwd_events=None):
+            if fwd_events:
+                fwd_events[0].record(stream)
+            dg.spmm(X, Y)
+            if fwd_events:
+                fwd_events[1].record(stream)
+            dg.spmm_t(Gm, Z)  # A^T G: A is symmetric, same partition and tiles
 
     for _ in range(args.warmup):
         step()
@@ -268,16 +328,33 @@ def run_ours(args, rank, world, local_rank):
     ms_per_step = ms / args.steps
     flops_step = 2 * (2.0 * nnz_total * F)
 
-    # end to end through the public API: pinned-host X, G -> device, both
-    # passes (halo exchange included), Y, Z -> pinned host, every step
-    hX = X.cpu().pin_memory()
-    hG = Gm.cpu().pin_memory()
-    hY = torch.empty_like(hX).pin_memory()
-    hZ = torch.empty_like(hG).pin_memory()
+    # end to end through the public API, every step: the rank's inputs from
+    # pinned host memory to the device (replicated mode: its row blocks of X and
+    # G, then an NCCL all-gather builds the full copies; exchange mode: its
+    # rows, the halo moving inside the passes), both passes, and its rows of
+    # Y, Z back to pinned host memory
+    if replicated:
+        hX = X[r0:r1].cpu().pin_memory()
+        hG = Gm[r0:r1].cpu().pin_memory()
+        bounds = W["bounds"]
+        xparts = [X[bounds[g]:bounds[g + 1]] for g in range(world)]
+        gparts = [Gm[bounds[g]:bounds[g + 1]] for g in range(world)]
+    else:
+        hX = X.cpu().pin_memory()
+        hG = Gm.cpu().pin_memory()
+    hY = torch.empty(tuple(Y.shape)).pin_memory()
+    hZ = torch.empty(tuple(Z.shape)).pin_memory()
 
     def e2e_step():
-        X.copy_(hX, non_blocking=True)
-        Gm.copy_(hG, non_blocking=True)
+        if replicated:
+            X[r0:r1].copy_(hX, non_blocking=True)
+            Gm[r0:r1].copy_(hG, non_blocking=True)
+            if world > 1:
+                dist.all_gather(xparts, X[r0:r1])
+                dist.all_gather(gparts, Gm[r0:r1])
+        else:
+            X.copy_(hX, non_blocking=True)
+            Gm.copy_(hG, non_blocking=True)
         step()
         hY.copy_(Y, non_blocking=True)
         hZ.copy_(Z, non_blocking=True)
@@ -304,7 +381,8 @@ def run_ours(args, rank, world, local_rank):
         return
     peak, peak_kind = measured_peaks()
     n_loc = dg.n_local
-    b_alg = 4 * F * (n_loc + n_loc) + 8 * dg.nnz + 4 * (n_loc + 1)
+    n_in = W["n"] if replicated else n_loc  # rows of X a rank's forward pass reads
+    b_alg = 4 * F * (n_in + n_loc) + 8 * dg.nnz + 4 * (n_loc + 1)
     achieved = b_alg / (fwd_ms * 1e-3) / 1e9
     # per SpMM: pull + zero pass on the local tiles; with a halo also the pack
     # kernel and pull + zero pass on the halo tiles
@@ -318,7 +396,7 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if replicated else "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded R-MAT, torch GPU generator seed 1)",
@@ -326,15 +404,19 @@ def run_ours(args, rank, world, local_rank):
                    "nnz_total": int(nnz_total), "nnz_rank0": dg.nnz, "F": F,
                    "halo_rows_total": int(halo_total), "tc_threshold": args.tc_threshold,
                    "l2": "inputs larger than L2 (X, G 512 MiB per GPU)",
-                   "parallelism": (f"{world}-way 1D row partition (nnz-balanced), compacted "
-                                   "halo all-to-all over NCCL overlapped with local tiles")
-                   if world > 1 else "1 GPU",
+                   "parallelism": ("1 GPU" if world == 1 else
+                                   f"{world}-way 1D row partition (nnz-balanced); X, G resident "
+                                   "on every GPU (all-gathered from the row blocks in the e2e leg)"
+                                   if replicated else
+                                   f"{world}-way 1D row partition (nnz-balanced), compacted "
+                                   "halo all-to-all over NCCL overlapped with local tiles"),
                    "convert_s": round(W["conv_s"], 3)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": profiled_traffic("pull_kernel_config2") if world == 1 else None,
                      "kernel": "pull_kernel, forward SpMM" + (" (local + halo tiles and the "
-                                                              "exchange)" if world > 1 else ""),
+                                                              "exchange)" if not replicated else
+                                                              " (rank 0's rows)" if world > 1 else ""),
                      "fwd_ms": round(fwd_ms, 4), "alg_bytes_per_launch": b_alg,
                      "peak_kind": peak_kind},
         "e2e": {"value": round(flops_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
