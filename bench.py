@@ -1,19 +1,26 @@
 """Benchmark of the tcc graph-aggregation hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload spmm|gcn4|config5] [--dist-mode replicated|exchange]
 
 Workload: seeded R-MAT graph, 2^20 nodes, 16M directed
 edges (a,b,c,d = 0.57,0.19,0.19,0.05) symmetrised, deduplicated, self-loops
 added; GCN normalisation D^-1/2 (A+I) D^-1/2 fused as diagonal scales; X, G
-fp32 [N x 128] ~ N(0,1).  One step = forward SpMM A.X over BCSR tiles plus the
-transposed SpMM A^T.G over BCSC tiles (the backward pass).  Metric: SpMM
-GFLOP/s = 2 nnz F per SpMM, whole job.
+fp32 [N x 128] ~ N(0,1).  One step = forward SpMM A.X plus the transposed SpMM
+A^T.G (the backward pass; A is symmetric, so both run over the BCSR tiles).
+Metric: SpMM GFLOP/s = 2 nnz F per SpMM, whole job.
 
-Multi-GPU (torchrun, one process per GPU): weak scaling -- the R-MAT scale grows
-with log2(N) (about 32 M nonzeros per GPU); the graph is row-partitioned with
-equal nonzeros, each SpMM exchanges the compacted feature halo with an NCCL
-all-to-all overlapped with the local-column tiles; rank 0 prints the line with
-the max time over ranks.
+Multi-GPU (torchrun, one process per GPU; rank 0 prints the line with the max
+time over ranks):
+  --dist-mode replicated (default): strong scaling -- the same config-2 job is
+      split into nnz-balanced row blocks; X and G are resident on every GPU
+      (the e2e leg copies each rank's row blocks from the host and all-gathers
+      them over NCCL every step);
+  --dist-mode exchange: weak scaling -- the R-MAT scale grows with log2(N)
+      (about 32 M nonzeros per GPU) and every SpMM exchanges the compacted
+      feature halo with an NCCL all-to-all overlapped with the local tiles.
+--workload gcn4 reports config 4's GCN epoch time (tcc_b200.train_gcn);
+--workload config5 the scale-26 forward SpMM (strong scaling).
 
 --impl reference: the reference path has no CPU implementation of its own (its
 SpMMs are CUDA kernels); this arm times the CPU restatement of the path
@@ -37,9 +44,14 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-WORKLOAD = ("config2 per GPU: R-MAT 2^(20+log2 N) nodes, 16 directed edges per node "
-            "symmetrised+dedup+self-loops, GCN-normalised, F=128, forward A.X + transposed "
-            "A^T.G over BCSR tiles")
+def workload_name(weak: bool) -> str:
+    if weak:
+        return ("config2 per GPU: R-MAT 2^(20+log2 N) nodes, 16 directed edges per node "
+                "symmetrised+dedup+self-loops, GCN-normalised, F=128, forward A.X + transposed "
+                "A^T.G over BCSR tiles, halo exchanged every step")
+    return ("config2: R-MAT 2^20 nodes, 16 directed edges per node symmetrised+dedup+self-loops, "
+            "GCN-normalised, F=128, forward A.X + transposed A^T.G over BCSR tiles; on N GPUs "
+            "split by rows with X and G resident on every GPU")
 
 
 def parse():
@@ -400,7 +412,7 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded R-MAT, torch GPU generator seed 1)",
-        "config": {"workload": WORKLOAD, "rmat_scale": scale, "nodes": W["n"],
+        "config": {"workload": workload_name(not replicated), "rmat_scale": scale, "nodes": W["n"],
                    "nnz_total": int(nnz_total), "nnz_rank0": dg.nnz, "F": F,
                    "halo_rows_total": int(halo_total), "tc_threshold": args.tc_threshold,
                    "l2": "inputs larger than L2 (X, G 512 MiB per GPU)",
@@ -577,7 +589,10 @@ def run_reference(args, rank, world, local_rank):
     import math
     import torch
     from tcc_b200 import graphs as G
-    scale = args.scale + int(round(math.log2(world)))
+    # our arm's workload: the config-2 graph at every N (strong scaling) by
+    # default, scale 20 + log2 N with --dist-mode exchange (weak scaling)
+    weak = args.dist_mode == "exchange" and world > 1
+    scale = args.scale + (int(round(math.log2(world))) if weak else 0)
     # the same graph as our arm (torch's CUDA and CPU generators draw different streams)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     rowptr, col, _ = G.rmat_gpu(scale, 16 << scale, seed=1, device=dev)
@@ -597,9 +612,9 @@ def run_reference(args, rank, world, local_rank):
     cb["value"] = value
     line = {"impl": "reference", "metric": "SpMM GFLOP/s (2*nnz*F)", "value": value,
             "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded R-MAT, torch generator seed 1)",
-            "config": {"workload": WORKLOAD, "rmat_scale": scale, "nodes": g.rows,
+            "higher_is_better": True, "scaling": "weak" if weak else "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded R-MAT, torch generator seed 1)",
+            "config": {"workload": workload_name(weak), "rmat_scale": scale, "nodes": g.rows,
                        "nnz": g.nnz, "F": 128},
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
