@@ -120,6 +120,15 @@ tcc_status tcc_swtcf_sizes(const tcc_swtcf* m, cudaStream_t stream, uint64_t* nu
  * superWindowSize == 16, like the reference. */
 tcc_status tcc_swtcf_spmm(const tcc_swtcf* m, const float* X, float* Y, uint32_t tc_threshold,
                           cudaStream_t stream);
+/* launchSWTCFSpMMQuantized (include/swtcf_spmm.cuh:18-26; src/swtcf_spmm.cu:
+ * 268-432, 469-502): Y[numDst x 128] += pattern(A) * Xq where source column c
+ * reads global node g = src_global[c] (NULL: g = c) and uses the int8 row
+ * q_x[g*128 .. g*128+127] times scales[g] in fp32; tiles with popcount >=
+ * tc_threshold use TF32 tensor cores, the others fp32.  Requires
+ * superWindowSize == 16, like the reference. */
+tcc_status tcc_swtcf_spmm_quantized(const tcc_swtcf* m, const int8_t* q_x, const float* scales,
+                                    const uint32_t* src_global, float* Y, uint32_t tc_threshold,
+                                    cudaStream_t stream);
 /* General form: any F (multiple of 4), row strides, diagonal scales fused
  * (Y = diag(row_scale) * A * diag(col_scale) * X, NULL = ones); accumulate = 0
  * overwrites Y (the reference always accumulates). */

@@ -20,6 +20,7 @@ u32p = np.ctypeslib.ndpointer(np.uint32, flags="C")
 u64p = np.ctypeslib.ndpointer(np.uint64, flags="C")
 u8p = np.ctypeslib.ndpointer(np.uint8, flags="C")
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
+i8p = np.ctypeslib.ndpointer(np.int8, flags="C")
 
 
 def build():
@@ -294,6 +295,9 @@ def ref_lib():
         L.ref_swtcf_spmm.restype = C.c_int
         L.ref_swtcf_spmm.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, u32p, u32p, f32p, f32p,
                                      C.c_uint32, C.c_int, C.c_int, C.POINTER(C.c_float)]
+        L.ref_swtcf_spmm_quantized.restype = C.c_int
+        L.ref_swtcf_spmm_quantized.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, u32p, u32p, i8p,
+                                               f32p, C.c_uint32, u32p, f32p, C.c_uint32]
         L.ref_cnic_spmm.restype = C.c_int
         L.ref_cnic_spmm.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                     u32p, u32p, u32p, u64p, C.c_uint32, C.c_uint32, u32p, u32p,
@@ -346,6 +350,20 @@ def ref_swtcf_spmm(rows, cols, dst, src, X128, tc_threshold=12, warmup=0, reps=0
     if rc != 0:
         raise OracleError(rc, L.ref_last_error().decode())
     return Y, (ms.value if reps > 0 else None)
+
+
+def ref_swtcf_spmm_quantized(rows, cols, dst, src, q_x, scales, src_global, tc_threshold=12):
+    """Reference convert + launchSWTCFSpMMQuantized on the GPU; returns Y."""
+    L = ref_lib()
+    Y = np.zeros((rows, 128), np.float32)
+    rc = L.ref_swtcf_spmm_quantized(rows, cols, len(dst), np.ascontiguousarray(dst, np.uint32),
+                                    np.ascontiguousarray(src, np.uint32),
+                                    np.ascontiguousarray(q_x, np.int8),
+                                    np.ascontiguousarray(scales, np.float32), q_x.shape[0],
+                                    np.ascontiguousarray(src_global, np.uint32), Y, tc_threshold)
+    if rc != 0:
+        raise OracleError(rc, L.ref_last_error().decode())
+    return Y
 
 
 def ref_cnic_spmm(num_rows, num_cols, B, bcsr=None, bcsc=None, warmup=0, reps=0):

@@ -10,7 +10,8 @@
 // Host buffers in, host buffers out: each call uploads, runs the reference entry
 // point (allocateDeviceSWTCF / allocateSWTCFConvertWorkspace / convertCOOToSWTCF,
 // include/swtcf_convert.cuh:74-78; launchSWTCFSpMM, include/swtcf_spmm.cuh:10-16)
-// and downloads.  Reference exceptions become return code -1 and a message.
+// and downloads (also launchSWTCFSpMMQuantized, include/swtcf_spmm.cuh:18-26).
+// Reference exceptions become return code -1 and a message.
 #include "swtcf_convert.cuh"
 #include "swtcf_spmm.cuh"
 
@@ -159,6 +160,65 @@ int ref_swtcf_spmm(uint32_t rows, uint32_t cols, uint32_t nnz, const uint32_t* d
     cudaFree(d_dst);
     cudaFree(d_src);
     cudaFree(d_x);
+    cudaFree(d_y);
+    return rc;
+}
+
+// Reference convert + launchSWTCFSpMMQuantized (include/swtcf_spmm.cuh:18-26):
+// q_x [n_global x 128] int8, scales [n_global], src_global [cols]; Y zeroed first.
+int ref_swtcf_spmm_quantized(uint32_t rows, uint32_t cols, uint32_t nnz, const uint32_t* dst,
+                             const uint32_t* src, const int8_t* q_x, const float* scales,
+                             uint32_t n_global, const uint32_t* src_global, float* Y,
+                             uint32_t tc_threshold) {
+    g_msg[0] = 0;
+    DeviceSWTCFMatrix m;
+    SWTCFConvertWorkspace ws;
+    uint32_t* d_dst = nullptr;
+    uint32_t* d_src = nullptr;
+    int8_t* d_q = nullptr;
+    float* d_s = nullptr;
+    uint32_t* d_g = nullptr;
+    float* d_y = nullptr;
+    int rc = 0;
+    try {
+        H_CHECK(cudaMalloc(&d_dst, sizeof(uint32_t) * nnz));
+        H_CHECK(cudaMalloc(&d_src, sizeof(uint32_t) * nnz));
+        H_CHECK(cudaMemcpy(d_dst, dst, sizeof(uint32_t) * nnz, cudaMemcpyHostToDevice));
+        H_CHECK(cudaMemcpy(d_src, src, sizeof(uint32_t) * nnz, cudaMemcpyHostToDevice));
+        allocateDeviceSWTCF(m, rows, cols, nnz, 16);
+        allocateSWTCFConvertWorkspace(ws, nnz, cols, 16);
+        convertCOOToSWTCF(d_dst, d_src, nnz, m, ws, 0);
+        H_CHECK(cudaDeviceSynchronize());
+        uint32_t derr = 0;
+        download(&derr, ws.deviceError, 1);
+        if (derr != 0) {
+            std::snprintf(g_msg, sizeof(g_msg), "reference converter device error %u", derr);
+            throw std::runtime_error(g_msg);
+        }
+        const std::size_t qe = (std::size_t)n_global * 128, ye = (std::size_t)rows * 128;
+        H_CHECK(cudaMalloc(&d_q, qe));
+        H_CHECK(cudaMalloc(&d_s, sizeof(float) * n_global));
+        H_CHECK(cudaMalloc(&d_g, sizeof(uint32_t) * cols));
+        H_CHECK(cudaMalloc(&d_y, ye * sizeof(float)));
+        H_CHECK(cudaMemcpy(d_q, q_x, qe, cudaMemcpyHostToDevice));
+        H_CHECK(cudaMemcpy(d_s, scales, sizeof(float) * n_global, cudaMemcpyHostToDevice));
+        H_CHECK(cudaMemcpy(d_g, src_global, sizeof(uint32_t) * cols, cudaMemcpyHostToDevice));
+        H_CHECK(cudaMemset(d_y, 0, ye * sizeof(float)));
+        launchSWTCFSpMMQuantized(m, d_q, d_s, d_g, d_y, tc_threshold, 0);
+        H_CHECK(cudaGetLastError());
+        H_CHECK(cudaDeviceSynchronize());
+        download(Y, d_y, ye);
+    } catch (const std::exception& e) {
+        if (!g_msg[0]) fail(e.what());
+        rc = -1;
+    }
+    freeSWTCFConvertWorkspace(ws);
+    freeDeviceSWTCF(m);
+    cudaFree(d_dst);
+    cudaFree(d_src);
+    cudaFree(d_q);
+    cudaFree(d_s);
+    cudaFree(d_g);
     cudaFree(d_y);
     return rc;
 }

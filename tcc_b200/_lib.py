@@ -77,6 +77,7 @@ PROTOTYPES = {
     "tcc_swtcf_workspace_device_error": (_st, [_vp, _vp, C.POINTER(_u32)]),
     "tcc_swtcf_sizes": (_st, [C.POINTER(Swtcf), _vp, C.POINTER(_u64), C.POINTER(_u64)]),
     "tcc_swtcf_spmm": (_st, [C.POINTER(Swtcf), _vp, _vp, _u32, _vp]),
+    "tcc_swtcf_spmm_quantized": (_st, [C.POINTER(Swtcf), _vp, _vp, _vp, _vp, _u32, _vp]),
     "tcc_swtcf_spmm_ex": (_st, [C.POINTER(Swtcf), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
                                 _i, _vp]),
     "tcc_swtcf_spmm_t": (_st, [C.POINTER(Swtcf), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i,

@@ -279,6 +279,21 @@ tcc_status tcc_swtcf_spmm(const tcc_swtcf* m, const float* X, float* Y, uint32_t
     });
 }
 
+tcc_status tcc_swtcf_spmm_quantized(const tcc_swtcf* m, const int8_t* q_x, const float* scales,
+                                    const uint32_t* src_global, float* Y, uint32_t tc_threshold,
+                                    cudaStream_t stream) {
+    return guarded("tcc_swtcf_spmm_quantized", [&] {
+        TCC_REQUIRE(m && q_x && scales && Y, "null argument");
+        TCC_REQUIRE(m->superWindowSize == 16, "Quantized SWTCF SpMM requires superWindowSize=16");
+        tcc::Dense d{nullptr, 128, Y, 128, 128, nullptr, nullptr};
+        d.qX = q_x;
+        d.ldq = 128;
+        d.qscale = scales;
+        d.qmap = src_global;
+        tcc::push_spmm(swtcf_push(m), d, tc_threshold, nullptr, stream);
+    });
+}
+
 tcc_status tcc_swtcf_spmm_ex(const tcc_swtcf* m, const float* X, uint64_t ldx, float* Y,
                              uint64_t ldy, uint32_t F, uint32_t tc_threshold,
                              const float* row_scale, const float* col_scale, int accumulate,

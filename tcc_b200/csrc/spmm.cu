@@ -344,6 +344,14 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
                     __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(xp), k);
                 if (cidx < a.num_in && fvalid)
                     x[k] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pv) + f);
+            } else if (d.qX) {
+                if (cidx < a.num_in && fvalid) {
+                    // dequantize like the reference: float(q) * scale[g] in fp32
+                    const uint32_t g = d.qmap ? __ldg(d.qmap + cidx) : cidx;
+                    const char4 q = __ldg(reinterpret_cast<const char4*>(d.qX + (uint64_t)g * d.ldq + f));
+                    const float sc = __ldg(d.qscale + g);
+                    x[k] = make_float4((float)q.x * sc, (float)q.y * sc, (float)q.z * sc, (float)q.w * sc);
+                }
             } else if (cidx < a.num_in && fvalid) {
                 x[k] = ld4(d.X + (uint64_t)cidx * d.ldx + f);
             }
@@ -532,9 +540,16 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
 void push_spmm(const PushTiles& a, const Dense& d, uint32_t tc_threshold, const FeatureStore* fs,
                cudaStream_t s) {
     TCC_REQUIRE(d.F > 0 && d.F % 4 == 0, "F must be a positive multiple of 4");
-    TCC_REQUIRE(d.ldx % 4 == 0 && d.ldy % 4 == 0 && d.ldx >= d.F && d.ldy >= d.F,
-                "row strides must be multiples of 4 elements and >= F");
-    TCC_REQUIRE(fs || ((uintptr_t)d.X % 16 == 0), "X must be 16-byte aligned");
+    TCC_REQUIRE(d.ldy % 4 == 0 && d.ldy >= d.F, "Y row stride must be a multiple of 4 and >= F");
+    if (d.qX) {
+        TCC_REQUIRE(!fs, "quantized rows and a feature store exclude each other");
+        TCC_REQUIRE(d.qscale && d.ldq % 4 == 0 && d.ldq >= d.F && (uintptr_t)d.qX % 4 == 0,
+                    "quantized X needs scales, a 4-byte aligned base and a row stride that is a "
+                    "multiple of 4 and >= F");
+    } else {
+        TCC_REQUIRE(d.ldx % 4 == 0 && d.ldx >= d.F, "X row stride must be a multiple of 4 and >= F");
+        TCC_REQUIRE(fs || ((uintptr_t)d.X % 16 == 0), "X must be 16-byte aligned");
+    }
     TCC_REQUIRE((uintptr_t)d.Y % 16 == 0, "Y must be 16-byte aligned");
     if (a.num_windows == 0) return;
     const unsigned gy = ceil_div(d.F, 128);

@@ -30,6 +30,13 @@ struct Dense {
     uint32_t F;
     const float* rs;
     const float* cs;
+    // int8 input rows instead of X (push pass only; launchSWTCFSpMMQuantized):
+    // input row c = float(qX[g * ldq + f]) * qscale[g], g = qmap[c] (qmap NULL:
+    // g = c)
+    const int8_t* qX = nullptr;
+    uint64_t ldq = 0;
+    const float* qscale = nullptr;
+    const uint32_t* qmap = nullptr;
 };
 
 // Hot/cold feature store of the mixed first-layer pass.

@@ -184,6 +184,31 @@ def spmm(m: SWTCFMatrix, X: torch.Tensor, Y: torch.Tensor,
     L.call("tcc_swtcf_spmm", C.byref(m.c), _ptr(X), _ptr(Y), tc_threshold, _stream(stream))
 
 
+def spmm_quantized(m: SWTCFMatrix, q_x: torch.Tensor, scales: torch.Tensor, src_global, Y: torch.Tensor,
+                   tc_threshold: int = DEFAULT_TC_THRESHOLD, stream=None):
+    """launchSWTCFSpMMQuantized (src/swtcf_spmm.cu:268-432, 469-502): Y += A Xq
+    with source column c reading int8 row q_x[src_global[c]] times
+    scales[src_global[c]] (src_global None: identity)."""
+    if q_x.dtype != torch.int8 or not q_x.is_cuda or q_x.shape[1] != FEATURE_DIM or \
+            q_x.stride(0) != FEATURE_DIM:
+        raise ValueError(f"q_x must be a contiguous CUDA int8 tensor with {FEATURE_DIM} columns")
+    if scales.dtype != torch.float32 or not scales.is_cuda or scales.dim() != 1 or \
+            not scales.is_contiguous() or scales.numel() < q_x.shape[0]:
+        raise ValueError("scales must be a contiguous CUDA float32 vector with one entry per q_x row")
+    _check_f32(Y, "Y")
+    if Y.shape[1] != FEATURE_DIM or Y.stride(0) != FEATURE_DIM:
+        raise ValueError(f"Y must be contiguous with {FEATURE_DIM} columns")
+    sg = None if src_global is None else src_global
+    if sg is not None and (sg.dtype != torch.int32 or not sg.is_cuda):
+        raise ValueError("src_global must be a CUDA int32 (uint32 bits) tensor")
+    L.call("tcc_swtcf_spmm_quantized", C.byref(m.c), _ptr(q_x), _ptr(scales), _ptr(sg), _ptr(Y),
+           tc_threshold, _stream(stream))
+
+
+# the reference's name
+launchSWTCFSpMMQuantized = spmm_quantized
+
+
 def spmm_ex(m: SWTCFMatrix, X: torch.Tensor, Y: torch.Tensor | None = None,
             tc_threshold: int = DEFAULT_TC_THRESHOLD, row_scale=None, col_scale=None,
             accumulate: bool = False, stream=None) -> torch.Tensor:

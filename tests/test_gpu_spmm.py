@@ -215,3 +215,29 @@ def test_full_size_properties(gpu):
     lhs = torch.sum(tiles.bcsr_spmm(bcsr, X1, tc_threshold=65).double() * Gm.double())
     rhs = torch.sum(X1.double() * tiles.bcsc_spmm_t(bcsc, Gm, tc_threshold=65).double())
     assert abs((lhs - rhs) / rhs).item() < 1e-5
+
+
+@pytest.mark.parametrize("name,g", CASES[:6], ids=[c[0] for c in CASES[:6]])
+@pytest.mark.parametrize("thr", [12, 0, 65])
+def test_swtcf_spmm_quantized(gpu, oracle, name, g, thr):
+    """launchSWTCFSpMMQuantized: source column c reads the int8 row of global node
+    src_global[c] times its scale; against the oracle on the dequantized rows
+    (the same fp32 values) and, where the reference build is present, against
+    the reference kernel."""
+    m = make_swtcf(g)
+    rng = np.random.default_rng(21)
+    n_global = g.cols + 37
+    q = rng.integers(-128, 128, size=(n_global, 128), dtype=np.int8)
+    scales = (rng.random(n_global, dtype=np.float32) * 0.05).astype(np.float32)
+    src_global = rng.permutation(n_global)[:g.cols].astype(np.uint32)
+    Xd = (q[src_global].astype(np.float32) * scales[src_global][:, None]).astype(np.float32)
+    Y = torch.zeros((g.rows, 128), dtype=torch.float32, device="cuda")
+    swtcf.spmm_quantized(m, torch.from_numpy(q).cuda(), torch.from_numpy(scales).cuda(),
+                         torch.from_numpy(src_global.view(np.int32)).cuda(), Y, tc_threshold=thr)
+    got = Y.cpu().numpy()
+    want = oracle.csr_spmm(g, Xd)
+    assert rel_fro(got, want) <= (FP32_TOL if thr > 64 else TF32_TOL), name
+    if oracle.ref_lib() is not None and g.nnz > 0:
+        dst, src = g.coo()
+        ref = oracle.ref_swtcf_spmm_quantized(g.rows, g.cols, dst, src, q, scales, src_global, thr)
+        assert rel_inf(got, ref) <= REF_TOL, name
