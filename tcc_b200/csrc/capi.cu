@@ -4,6 +4,8 @@
 #include "convert.cuh"
 #include "spmm.cuh"
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <mutex>
 #include <string>
 
@@ -19,8 +21,16 @@ struct tcc_tiles_workspace {
 namespace {
 thread_local std::string g_last_error;
 
+// Every C-ABI call runs inside an NVTX range named after it (visible in
+// Nsight timelines; a no-op when no tool is attached).
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
+
 template <typename Fn>
 tcc_status guarded(const char* where, Fn&& fn) {
+    NvtxRange range(where);
     try {
         fn();
         return TCC_OK;

@@ -188,21 +188,24 @@ class DistGraph:
         from . import tiles
         from . import _lib as L
         X_local = X_local.contiguous()
-        halo, work = self.exchange(X_local)
+        with torch.cuda.nvtx.range("tcc.halo_exchange_start"):
+            halo, work = self.exchange(X_local)
         # leave SMs for the exchange's NCCL kernels while the local tiles run
         reserve = self.comm_sms if work is not None else 0
         prev = L.lib().tcc_get_grid_reserve()
         L.lib().tcc_set_grid_reserve(reserve)
         try:
-            Y = tiles.bcsr_spmm(self.tiles_loc, X_local, out, tc_threshold=self.tc_threshold,
-                                rs=self.rs, cs=self.cs_local)
+            with torch.cuda.nvtx.range("tcc.local_tiles"):
+                Y = tiles.bcsr_spmm(self.tiles_loc, X_local, out, tc_threshold=self.tc_threshold,
+                                    rs=self.rs, cs=self.cs_local)
         finally:
             L.lib().tcc_set_grid_reserve(prev)
         if work is not None:
             work.wait()
         if self.tiles_halo is not None:
-            tiles.bcsr_spmm(self.tiles_halo, halo, Y, tc_threshold=self.tc_threshold, rs=self.rs,
-                            cs=self.cs_halo, accumulate=True)
+            with torch.cuda.nvtx.range("tcc.halo_tiles"):
+                tiles.bcsr_spmm(self.tiles_halo, halo, Y, tc_threshold=self.tc_threshold,
+                                rs=self.rs, cs=self.cs_halo, accumulate=True)
         return Y
 
     # A symmetric (every BASELINE graph): Aᵀ·G on the same partition is A·G.

@@ -19,7 +19,9 @@ own rows:
   collectives run in the same order as its halo exchanges), then Adam.
 
 ``transform_first`` computes layer 2 as Â·(H1·W2) (47 wide instead of 256; the
-reference always aggregates first).
+reference always aggregates first).  ``--save`` / ``--resume`` write and read a
+checkpoint of the weights, the Adam state and the epoch count (the reference
+saves none).
 
 Run: ``python -m tcc_b200.train_gcn`` (1 GPU) or under torch.distributed.run.
 """
@@ -120,6 +122,14 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool = Fals
     W2.requires_grad_(True)
     params = [W1, W2]
     opt = torch.optim.Adam(params, lr=cfg["lr"])
+    start_epoch = 0
+    if cfg.get("resume"):
+        ck = torch.load(cfg["resume"], map_location=device)
+        with torch.no_grad():
+            W1.copy_(ck["W1"])
+            W2.copy_(ck["W2"])
+        opt.load_state_dict(ck["opt"])
+        start_epoch = int(ck["epoch"])
     drop = torch.Generator(device=device)
     drop.manual_seed(cfg["seed"] * 1000 + rank)
     cls_pad = (cfg["classes"] + 3) // 4 * 4  # transform-first SpMM width, multiple of 4
@@ -152,7 +162,7 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool = Fals
         return lt
 
     times, losses = [], []
-    for _ in range(cfg["epochs"]):
+    for _ in range(start_epoch, cfg["epochs"]):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -164,7 +174,12 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool = Fals
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b) / 1e3)
         losses.append(float(lt))
-    t = torch.tensor(times, device=device)
+    if cfg.get("save") and rank == 0:  # weights are identical on every rank
+        torch.save({"W1": W1.detach(), "W2": W2.detach(), "opt": opt.state_dict(),
+                    "epoch": cfg["epochs"], "config": {k: v for k, v in cfg.items()
+                                                       if k not in ("save", "resume")}},
+                   cfg["save"])
+    t = torch.tensor(times or [0.0], device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     nnz = torch.tensor([float(R["nnz"])], device=device, dtype=torch.float64)
@@ -193,6 +208,8 @@ def main(argv=None):
     p.add_argument("--shrink", type=int, default=0, help="divide nodes and edges by 2**shrink")
     p.add_argument("--epochs", type=int, default=10)
     p.add_argument("--transform-first", action="store_true")
+    p.add_argument("--save", default=None, help="checkpoint path written at the end (rank 0)")
+    p.add_argument("--resume", default=None, help="checkpoint to continue from")
     a = p.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -205,6 +222,7 @@ def main(argv=None):
     try:
         cfg = config(a.shrink)
         cfg["epochs"] = a.epochs
+        cfg["save"], cfg["resume"] = a.save, a.resume
         r = train(cfg, device, world, rank, a.transform_first)
         if rank == 0:
             steady = r["epoch_s"][1:] or r["epoch_s"]

@@ -52,3 +52,18 @@ def test_gcn_trainer_matches_dense_reference(gpu, transform_first):
     want = _dense_loss(cfg, dev)
     assert abs(r["losses"][0] - want) / want <= 2e-3, (r["losses"][0], want)
     assert r["losses"][-1] < r["losses"][0]
+
+
+def test_gcn_checkpoint_resume_continues_the_run(gpu, tmp_path):
+    """6 epochs in one go == 3 epochs, checkpoint, 3 more from the checkpoint
+    (dropout off, so the runs are deterministic up to kernel rounding)."""
+    cfg = train_gcn.config(shrink=10)
+    cfg["dropout"] = 0.0
+    dev = torch.device("cuda", 0)
+    full = train_gcn.train(dict(cfg, epochs=6), dev, 1, 0)
+    ck = str(tmp_path / "gcn.pt")
+    first = train_gcn.train(dict(cfg, epochs=3, save=ck), dev, 1, 0)
+    rest = train_gcn.train(dict(cfg, epochs=6, resume=ck), dev, 1, 0)
+    assert len(rest["losses"]) == 3
+    got = first["losses"] + rest["losses"]
+    assert max(abs(a - b) / b for a, b in zip(got, full["losses"])) < 1e-4
