@@ -5,27 +5,30 @@
 // 1560-1843, and the transposed pass that replaces torch.sparse.mm(A_topo.T, .)
 // at train/tcgnn_conv_release.py:152), with a different data path:
 //
-// * Work split: the tile range [0, T) is cut into G equal pieces, one per warp
-//   (G = CTAs x warps).  A warp walks the windows that meet its piece in order
-//   and keeps the window's 8 x F-slice partial sums in registers, so a window
-//   is written once with plain stores.  Windows cut by a piece boundary, and
+// * Work split: the tile range [0, T) is cut into G = kPieces x (CTAs x warps)
+//   equal pieces; warp g takes pieces g, g + CTAs x warps, ..., so every warp
+//   sees hub-heavy and many-small-window regions alike.  A warp walks the
+//   windows that meet a piece in order and keeps the window's 8 x F-slice
+//   partial sums in registers, so a window is written once with plain stores.  Windows cut by a piece boundary, and
 //   windows longer than kFlushTiles tiles (whose warp flushes every
 //   kFlushTiles tiles to keep fp32 sums short), are zeroed first and reduced
 //   with red.global.add.v4.
 // * Gathers: each real feature row of a tile (up to 8 x 512 B) is fetched by
 //   one bulk async copy (the TMA unit's cp.async.bulk) into a per-warp ring of
-//   kR shared-memory stages completed through mbarriers.  This keeps the row
-//   gathers off the LSU/L1 fill path, where every missed 32-byte sector costs
-//   a data-pipe wavefront.  Rows sit 32 bytes apart beyond their length, so
-//   the MMA fragment loads (4 rows x 8 float4 per quarter-warp) hit 8 distinct
-//   bank groups.
-// * Arithmetic: the tensor-core tile product of tile_mma_scaled -- TF32 for
-//   tiles with popcount >= tc_threshold (the reference's dense-tile
-//   arithmetic), an fp32-level TF32 split for the others -- with the column
-//   scale folded into the B operand.
-// * Metadata (gather indices, bitmaps, column scales) runs three 16-tile
-//   batches ahead in registers, so neither the index stream nor the dependent
-//   scale loads stall the warp.
+//   kR shared-memory stages completed through mbarriers; the 8 rows of a tile
+//   are issued by 8 lanes in one instruction.  This keeps the row gathers off
+//   the LSU/L1 fill path, where every missed 32-byte sector costs a data-pipe
+//   wavefront (measured on B200: register gathers top out near 32 B/clk/SM
+//   from L2, bulk copies above 48).  Rows sit 32 bytes apart beyond their
+//   length, so the MMA fragment loads (4 rows x 2 float4 per quarter-warp) hit
+//   distinct banks.
+// * Arithmetic: the register-gather kernel's (tile_mma): X rows scaled by the
+//   column scale in fp32, then TF32 rounded like cvt.rna for tiles with
+//   popcount >= tc_threshold (the reference's dense-tile arithmetic) and the
+//   fp32-level hi/lo TF32 split for the others.
+// * Metadata (gather indices, bitmaps, column scales) runs three 4-tile
+//   batches ahead in registers, one lane per gathered row, so neither the
+//   index stream nor the dependent scale loads stall the warp.
 //
 // Every mbarrier wait is bounded by %globaltimer; on expiry the kernel records
 // TCC_DEVERR_WAIT_TIMEOUT, waits (bounded) for its own copies in flight
@@ -42,21 +45,26 @@ namespace tcc {
 
 namespace {
 
-constexpr int kTW = 12;                          // warps per CTA
-constexpr int kR = 4;                            // ring stages per warp
+constexpr int kTW = 16;                          // warps per CTA
+constexpr int kR = 3;                            // ring stages per warp
 constexpr uint32_t kMaxBox = 128;                // floats per gathered row segment
 constexpr uint32_t kRowPad = 32;                 // bytes between rows beyond their length
 constexpr uint32_t kStageBytes = 8 * (kMaxBox * 4 + kRowPad);
-constexpr uint32_t kBatch = 16;                  // tiles per metadata batch
+constexpr uint32_t kBatch = 4;                   // tiles per metadata batch (8 lanes each)
 constexpr uint32_t kFlushTiles = 64;             // max tiles summed in one fp32 register chain
+constexpr uint32_t kPieces = 8;                  // tile-range pieces per warp
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 struct __align__(16) StageMeta {
-    float cs[8];              // column scale of gathered row k (0 for padding); 16-byte stores
-    unsigned long long bits;  // output-major bitmap: bit r*8 + k
-    uint32_t valid;           // bit k: gathered row k holds a real column (others are stale)
-    uint32_t pad[5];
+    float cs[8];              // column scale of gathered row k (0 for padding) at
+                              // [2 * (k % 4) + k / 4]: lane tig reads rows tig, tig + 4 at once
+    unsigned long long bits;  // output-major bitmap: bit r*8 + k, padding columns cleared
+    uint32_t pad[6];
 };
+
+// Source of the stage rows of padding columns: every stage row is written
+// by one copy, so padding rows hold zeros, never stale data.
+__device__ __align__(16) float g_zero_row[kMaxBox];
 static_assert(sizeof(StageMeta) == 64 && offsetof(StageMeta, cs) == 0,
               "stage metadata: 64 bytes, column scales 16-byte aligned");
 
@@ -73,14 +81,17 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
+// One try_wait on phase `parity`; the warp may sleep up to kSuspendNs inside
+// the instruction until the phase completes (no spinning on the issue slots).
+constexpr uint32_t kSuspendNs = 200000;
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "n"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -114,11 +125,9 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
         : "memory");
 }
 
-__device__ __forceinline__ uint4 ld_nc_v4(const uint32_t* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
+__device__ __forceinline__ uint32_t ld_nc_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
 
@@ -153,12 +162,13 @@ __device__ __forceinline__ uint32_t warp_lower_bound(uint32_t lo, uint32_t hi, P
     return b ? lo + __ffs(b) - 1 : hi;
 }
 
-// Metadata of one 16-tile batch as held by a lane: tile base + lane/2, gather
-// rows 4*(lane&1) .. +3.
+// Metadata of one 4-tile batch as held by a lane: tile base + lane/8, gather
+// row lane%8.  After finish(): bits in output-major form with padding
+// columns cleared.
 struct Batch {
-    uint4 idx;
+    uint32_t idx;
+    float cs;
     unsigned long long bits;
-    float4 cs;
 };
 
 // Window w is "reduced" -- its rows are written with red.global.add into rows
@@ -191,7 +201,8 @@ __global__ void zero_reduced_kernel(const uint32_t* __restrict__ off, uint32_t W
     }
 }
 
-template <int NP>
+// FULL: bw == 64 * NP (every float4 slot of the warp is a real feature).
+template <int NP, bool FULL>
 __global__ void __launch_bounds__(kTW * 32, 1)
     pull_tma_kernel(PullTiles a, Dense d, uint32_t bw, uint32_t thr, int accumulate,
                     uint32_t* __restrict__ err) {
@@ -210,66 +221,48 @@ __global__ void __launch_bounds__(kTW * 32, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncwarp();
 
-    const uint32_t rowbytes = bw * 4;
+    const uint32_t rowbytes = FULL ? 256 * NP : bw * 4;
     const uint32_t pitch = rowbytes + kRowPad;
     const int32_t fb = (int32_t)(blockIdx.y * kMaxBox);
     const int gid = lane >> 2, tig = lane & 3;
-    const uint64_t G = (uint64_t)gridDim.x * kTW;
-    const uint64_t g = (uint64_t)blockIdx.x * kTW + wib;
+    // piece p = g + j * GW of the kPieces * GW equal tile pieces; a warp's
+    // pieces are spread over the whole matrix, so hub-heavy and
+    // many-small-window regions share out evenly across warps
+    const uint64_t GW = (uint64_t)gridDim.x * kTW;
+    const uint64_t G = GW * kPieces;
+    const uint64_t g0 = (uint64_t)blockIdx.x * kTW + wib;
     const uint32_t T = a.num_tiles, W = a.num_windows;
-    const uint32_t T0 = (uint32_t)(g * T / G), T1 = (uint32_t)((g + 1) * T / G);
     const uint32_t* off = a.win_offset;
-
-    // windows meeting [T0, T1): first w with off[w+1] > T0 or off[w] >= T0,
-    // up to the first window starting at or after T1 (all remaining for the
-    // last warp, so trailing empty windows are written)
-    const uint32_t wb = warp_lower_bound(
-        0, W, [&](uint32_t w) { return off[w + 1] > T0 || off[w] >= T0; }, lane);
-    const uint32_t we =
-        g + 1 == G ? W : warp_lower_bound(wb, W, [&](uint32_t w) { return off[w] >= T1; }, lane);
+    uint32_t T0 = 0, T1 = 0;  // tile range of the current piece
 
     // ---- metadata pipeline: B0 current (complete), B1 (cs in flight), B2 (idx in flight)
+    const int grp = lane >> 3, krow = lane & 7;
     auto load_idx = [&](uint32_t base, Batch& b) {
-        const uint32_t t = base + (lane >> 1);
-        b.idx = make_uint4(kInvalid, kInvalid, kInvalid, kInvalid);
+        const uint32_t t = base + grp;
+        b.idx = kInvalid;
         b.bits = 0;
         if (t < T1) {
-            b.idx = ld_nc_v4(a.idx + (uint64_t)t * 8 + 4 * (lane & 1));
+            b.idx = ld_nc_u32(a.idx + (uint64_t)t * 8 + krow);
             b.bits = ld_nc_u64(a.bits + t);
         }
     };
     auto load_cs = [&](Batch& b) {
-        auto one = [&](uint32_t k) {
-            return k < a.num_in ? (d.cs ? __ldg(d.cs + k) : 1.f) : 0.f;
-        };
-        b.cs = make_float4(one(b.idx.x), one(b.idx.y), one(b.idx.z), one(b.idx.w));
+        b.cs = b.idx < a.num_in ? (d.cs ? __ldg(d.cs + b.idx) : 1.f) : 0.f;
     };
-    // bitmap to output-major form, padding columns cleared; returns the
-    // tile's valid-row mask (bit k: gather row k is a real column)
-    auto finish = [&](Batch& b) -> uint32_t {
+    auto finish = [&](Batch& b) {
         unsigned long long bits = b.bits;
         if (a.bits_transposed) bits = transpose8x8(bits);
-        const uint32_t n_in = a.num_in;
-        uint32_t vmask = (b.idx.x < n_in ? 1u : 0u) | (b.idx.y < n_in ? 2u : 0u) |
-                         (b.idx.z < n_in ? 4u : 0u) | (b.idx.w < n_in ? 8u : 0u);
-        vmask <<= 4 * (lane & 1);
-        vmask |= __shfl_xor_sync(0xffffffffu, vmask, 1);
-        b.bits = bits & (0x0101010101010101ull * (unsigned long long)vmask);
-        return vmask;
+        const unsigned vm = __ballot_sync(0xffffffffu, b.idx < a.num_in);
+        const uint32_t valid = (vm >> (8 * grp)) & 0xFFu;
+        b.bits = bits & (0x0101010101010101ull * (unsigned long long)valid);
     };
 
     Batch B0, B1, B2;
-    uint32_t vmask = 0;
-    uint32_t mb = T0;
-    if (T0 < T1) {
-        load_idx(T0, B0);
-        load_idx(T0 + kBatch, B1);
-        load_idx(T0 + 2 * kBatch, B2);
-        load_cs(B0);
-        load_cs(B1);
-        vmask = finish(B0);
-    }
+    uint32_t mb = 0;
+    uint32_t iq = 0;            // ring slot of the next issued tile
+    uint32_t cq = 0, cpar = 0;  // ring slot and phase parity of the next consumed tile
 
+    // tiles are issued in order, one ring slot after another, across pieces
     auto issue = [&](uint32_t t) {
         if (t >= mb + kBatch) {  // rotate (uniform: t is the same in every lane)
             B0 = B1;
@@ -277,46 +270,37 @@ __global__ void __launch_bounds__(kTW * 32, 1)
             mb += kBatch;
             load_cs(B1);
             load_idx(mb + 2 * kBatch, B2);
-            vmask = finish(B0);
+            finish(B0);
         }
-        const uint32_t j = t - mb;
-        if ((uint32_t)(lane >> 1) == j) {
-            const uint32_t q = (t - T0) % kR;
+        const uint32_t q = iq;
+        if (++iq == (uint32_t)kR) iq = 0;
+        if ((uint32_t)grp == t - mb) {
             const uint32_t bar = smem_u32(&sbar[q]);
-            const int h = lane & 1;
             StageMeta& m = smeta[q];
-            if (h == 0) {
-                m.bits = B0.bits;
-                m.valid = vmask;
-                *reinterpret_cast<float4*>(&m.cs[0]) = B0.cs;
-            } else {
-                *reinterpret_cast<float4*>(&m.cs[4]) = B0.cs;
-            }
+            m.cs[2 * (krow & 3) + (krow >> 2)] = B0.cs;
+            if (krow == 0) m.bits = B0.bits;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            if (h == 0) mbar_arrive_tx(bar, (uint32_t)__popc(vmask) * rowbytes);
-            // real rows of this lane's half; padding rows are not fetched
-            const uint32_t dst = smem_u32(sdata + q * kStageBytes) + 4 * h * pitch;
-            const uint32_t rows[4] = {B0.idx.x, B0.idx.y, B0.idx.z, B0.idx.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                if ((vmask >> (4 * h + e)) & 1u)
-                    bulk_copy(dst + e * pitch, d.X + (uint64_t)rows[e] * d.ldx + fb, rowbytes, bar);
+            // the transaction count may run ahead of expect_tx (it goes
+            // negative); the phase cannot complete before this arrival
+            if (krow == 0) mbar_arrive_tx(bar, 8 * rowbytes);
+            const float* row = B0.idx < a.num_in ? d.X + (uint64_t)B0.idx * d.ldx + fb : g_zero_row;
+            bulk_copy(smem_u32(sdata + q * kStageBytes) + krow * pitch, row, rowbytes, bar);
         }
     };
 
     // window offsets, 32 at a time
-    uint32_t ob = wb;
-    uint32_t offv = wb + lane <= W ? off[wb + lane] : 0;
+    uint32_t ob = 0, offv = 0;
     auto off_at = [&](uint32_t i) -> uint32_t {  // uniform i, ob <= i < ob + 32
         return __shfl_sync(0xffffffffu, offv, (int)(i - ob));
     };
-
-    uint32_t t = T0;
-    for (uint32_t p = T0; p < T1 && p < T0 + kR; ++p) issue(p);
-    __syncwarp();  // stage metadata written by the issuing lanes
+    // row scales of window w: lane r < 8 holds rs of row 8w + r
+    auto load_rs = [&](uint32_t w) -> float {
+        const uint32_t row = w * 8 + lane;
+        return (d.rs && lane < 8 && row < a.num_out) ? __ldg(d.rs + row) : 1.f;
+    };
 
     // Write (or reduce) a window's partial sums: lane holds output rows 2tig,
-    // 2tig+1 at float4 slots gid + 8s.  rsv: lane r < 8 holds rs of row r.
+    // 2tig+1 at float4 slots gid + 8s.
     uint32_t row0 = 0;
     float rsv = 1.f;
     auto emit = [&](float (&acc)[4 * NP][4], bool red) {
@@ -329,7 +313,7 @@ __global__ void __launch_bounds__(kTW * 32, 1)
 #pragma unroll
             for (int sl = 0; sl < 2 * NP; ++sl) {
                 const uint32_t f = 4 * (gid + 8 * sl);
-                if (f >= bw) continue;
+                if (!FULL && f >= bw) continue;
                 const int p = sl >> 1, e = (sl & 1) * 2 + h;
                 float4 v = make_float4(acc[4 * p + 0][e], acc[4 * p + 1][e], acc[4 * p + 2][e],
                                        acc[4 * p + 3][e]);
@@ -347,73 +331,114 @@ __global__ void __launch_bounds__(kTW * 32, 1)
     };
 
     bool failed = false;
-    for (uint32_t w = wb; w < we && !failed; ++w) {
-        if (w + 1 >= ob + 32) {
-            ob = w;
-            offv = ob + lane <= W ? off[ob + lane] : 0;
+    uint32_t t = 0, fq = 0, fpar = 0;  // on failure: tile t waited on slot fq, parity fpar
+    for (uint32_t j = 0; j < kPieces && !failed; ++j) {
+        const uint64_t piece = g0 + j * GW;
+        T0 = (uint32_t)(piece * T / G);
+        T1 = (uint32_t)((piece + 1) * T / G);
+        // windows meeting [T0, T1): first w with off[w+1] > T0 or off[w] >= T0,
+        // up to the first window starting at or after T1 (all remaining for
+        // the last piece, so trailing empty windows are written)
+        const uint32_t wb = warp_lower_bound(
+            0, W, [&](uint32_t w) { return off[w + 1] > T0 || off[w] >= T0; }, lane);
+        const uint32_t we =
+            piece + 1 == G ? W : warp_lower_bound(wb, W, [&](uint32_t w) { return off[w] >= T1; }, lane);
+
+        mb = T0;
+        if (T0 < T1) {
+            load_idx(T0, B0);
+            load_idx(T0 + kBatch, B1);
+            load_idx(T0 + 2 * kBatch, B2);
+            load_cs(B0);
+            load_cs(B1);
+            finish(B0);
         }
-        const uint32_t o0 = off_at(w), o1 = off_at(w + 1);
-        const uint32_t te = min(o1, T1);
-        const bool reduced = o0 < T0 || o1 > T1 || o1 - o0 > kFlushTiles;
-        row0 = w * 8;
-        rsv = (d.rs && lane < 8 && row0 + lane < a.num_out) ? __ldg(d.rs + row0 + lane) : 1.f;
-        uint32_t chain = 0;
+        ob = wb;
+        offv = wb + lane <= W ? off[wb + lane] : 0;
+        t = T0;
+        for (uint32_t u = T0; u < T1 && u < T0 + kR; ++u) issue(u);
+        __syncwarp();  // stage metadata written by the issuing lanes
+        float rs_next = wb < we ? load_rs(wb) : 1.f;
 
-        float dacc[4 * NP][4];
-#pragma unroll
-        for (int j = 0; j < 4 * NP; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
-
-        for (; t < te; ++t) {
-            const uint32_t q = (t - T0) % kR;
-            const uint32_t par = ((t - T0) / kR) & 1u;
-            bool ok = mbar_try(smem_u32(&sbar[q]), par);
-            if (!__all_sync(0xffffffffu, ok)) ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sbar[q]), par));
-            if (!ok) {
-                failed = true;
-                break;
+        for (uint32_t w = wb; w < we; ++w) {
+            if (w + 1 >= ob + 32) {
+                ob = w;
+                offv = ob + lane <= W ? off[ob + lane] : 0;
             }
-            const StageMeta& m = smeta[q];
-            const unsigned long long bits = m.bits;
-            const uint32_t valid = m.valid;
-            const float c0 = m.cs[tig], c1 = m.cs[tig + 4];
-            const unsigned char* src = sdata + q * kStageBytes;
-            // fragment-order rows k = tig + 4r, float4 slots 4*(gid + 8s) (tile_mma)
-            float4 x[2][2 * NP];
+            const uint32_t o0 = off_at(w), o1 = off_at(w + 1);
+            const uint32_t te = min(o1, T1);
+            const bool reduced = o0 < T0 || o1 > T1 || o1 - o0 > kFlushTiles;
+            row0 = w * 8;
+            rsv = rs_next;
+            if (w + 1 < we) rs_next = load_rs(w + 1);  // one window ahead
+            uint32_t chain = 0;
+
+            float dacc[4 * NP][4];
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int k = tig + 4 * r;
-                // rows of padding columns were never written: zero them, or
-                // 0 * NaN could reach the accumulators
-                const bool ok = (valid >> k) & 1u;
+            for (int k = 0; k < 4 * NP; ++k) dacc[k][0] = dacc[k][1] = dacc[k][2] = dacc[k][3] = 0.f;
+
+            for (; t < te; ++t) {
+                const uint32_t q = cq;
+                const uint32_t par = cpar;
+                if (++cq == (uint32_t)kR) {
+                    cq = 0;
+                    cpar ^= 1u;
+                }
+                bool ok = mbar_try(smem_u32(&sbar[q]), par);
+                if (!__all_sync(0xffffffffu, ok))
+                    ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sbar[q]), par));
+                if (!ok) {
+                    failed = true;
+                    fq = q;
+                    fpar = par;
+                    break;
+                }
+                const StageMeta& m = smeta[q];
+                const unsigned long long bits = m.bits;
+                const float2 cc = *reinterpret_cast<const float2*>(&m.cs[2 * tig]);
+                const float c[2] = {cc.x, cc.y};
+                const unsigned char* src = sdata + q * kStageBytes;
+                // fragment-order rows k = tig + 4r, float4 slots 4*(gid + 8s) (tile_mma),
+                // scaled by the column scale like the register-gather kernel
+                float4 x[2][2 * NP];
 #pragma unroll
-                for (int sl = 0; sl < 2 * NP; ++sl) {
-                    const uint32_t f = 4 * (gid + 8 * sl);
-                    x[r][sl] = ok && f < bw ? *reinterpret_cast<const float4*>(src + k * pitch + 4 * f)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < 2; ++r)
+#pragma unroll
+                    for (int sl = 0; sl < 2 * NP; ++sl) {
+                        const uint32_t f = 4 * (gid + 8 * sl);
+                        x[r][sl] = FULL || f < bw
+                                       ? f4_scale(*reinterpret_cast<const float4*>(
+                                                      src + (tig + 4 * r) * pitch + 4 * f),
+                                                  c[r])
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                __syncwarp();
+                if (t + kR < T1) issue(t + kR);
+                tile_mma<NP>(dacc, x, bits, gid, tig, (uint32_t)__popcll(bits) < thr);
+                if (++chain == kFlushTiles && t + 1 < te) {  // reduced windows only
+                    emit(dacc, true);
+#pragma unroll
+                    for (int k = 0; k < 4 * NP; ++k) dacc[k][0] = dacc[k][1] = dacc[k][2] = dacc[k][3] = 0.f;
+                    chain = 0;
                 }
             }
-            __syncwarp();
-            if (t + kR < T1) issue(t + kR);
-            tile_mma_scaled<NP>(dacc, x, bits, c0, c1, gid, tig, (uint32_t)__popcll(bits) < thr,
-                                d.cs != nullptr);
-            if (++chain == kFlushTiles && t + 1 < te) {  // reduced windows only
-                emit(dacc, true);
-#pragma unroll
-                for (int j = 0; j < 4 * NP; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
-                chain = 0;
-            }
-        }
-        if (failed) break;
+            if (failed) break;
 
-        emit(dacc, reduced);
+            emit(dacc, reduced);
+        }
     }
 
     if (failed) {
         if (lane == 0) atomicExch(err, (uint32_t)TCC_DEVERR_WAIT_TIMEOUT);
-        // copies still in flight: tiles issued (t .. min(T1, t+kR)) not consumed
+        // copies still in flight: tiles t .. min(T1, t + kR) - 1 were issued and
+        // not consumed, in ring order from slot fq
+        uint32_t q = fq, par = fpar;
         for (uint32_t u = t; u < T1 && u < t + kR; ++u) {
-            const uint32_t q = (u - T0) % kR;
-            (void)mbar_wait(smem_u32(&sbar[q]), ((u - T0) / kR) & 1u);
+            (void)mbar_wait(smem_u32(&sbar[q]), par);
+            if (++q == (uint32_t)kR) {
+                q = 0;
+                par ^= 1u;
+            }
         }
     }
 }
@@ -421,9 +446,7 @@ __global__ void __launch_bounds__(kTW * 32, 1)
 }  // namespace
 
 bool pull_tma_eligible(const PullTiles& a, const Dense& d) {
-    // opt-in (TCC_PULL_KERNEL=tma): measured slower than the register-gather
-    // kernel on the power-law configs (instruction-bound, ~345 instructions
-    // per tile against ~250)
+    // opt-in (TCC_PULL_KERNEL=tma)
     const char* e = std::getenv("TCC_PULL_KERNEL");
     if (!e || std::strcmp(e, "tma") != 0 || a.sw_rows) return false;
     if (d.F % 4 != 0 || (d.F > kMaxBox && d.F % kMaxBox != 0)) return false;
@@ -436,11 +459,14 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
     const uint32_t bw = d.F <= kMaxBox ? d.F : kMaxBox;
     const uint32_t slices = d.F <= kMaxBox ? 1 : d.F / kMaxBox;
     const uint32_t ctas = (uint32_t)grid_sms();
-    const uint32_t G = ctas * kTW;
+    const uint32_t G = ctas * kTW * kPieces;
     if (!accumulate && a.num_tiles > 0)
         zero_reduced_kernel<<<std::min<unsigned>(ceil_div(a.num_windows, 8), ctas * 8), 256, 0, s>>>(
             a.win_offset, a.num_windows, a.num_tiles, G, d.Y, d.ldy, d.F, a.num_out);
-    auto k = bw <= 64 ? pull_tma_kernel<1> : pull_tma_kernel<2>;
+    auto k = bw == 128  ? pull_tma_kernel<2, true>
+             : bw == 64 ? pull_tma_kernel<1, true>
+             : bw < 64  ? pull_tma_kernel<1, false>
+                        : pull_tma_kernel<2, false>;
     TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(a, d, bw, thr, accumulate, err);
     TCC_CUDA(cudaGetLastError());

@@ -151,17 +151,17 @@ def test_bcsr_pull(gpu, oracle, pull_kernel, name, g, F, thr):
 @pytest.mark.parametrize("kernel", ["ldg", "tma", "umma"])
 def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle, monkeypatch, kernel):
     """TF32 on every tile (tc_threshold 0) against its exact restatement: the
-    register-gather kernel rounds X like cvt.rna (the oracle's tile
-    emulation); the bulk-copy and tcgen05 kernels hand the tensor core raw
-    fp32 bits and it drops the low 13 mantissa bits, i.e. A.trunc(X) summed
-    in fp32.  The device error word stays clear."""
+    register-gather and bulk-copy kernels round X like cvt.rna (the oracle's
+    tile emulation); the tcgen05 kernel hands the tensor core raw fp32 bits
+    and it drops the low 13 mantissa bits, i.e. A.trunc(X) summed in fp32.
+    The device error word stays clear."""
     monkeypatch.setenv("TCC_PULL_KERNEL", kernel)
     g = G.sbm(2000, 20, 120000, 40.0, 1.2, seed=12)
     rp, col = csr_dev(g)
     t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
     X = G.features(g.cols, 128, seed=9)
     Y = tiles.bcsr_spmm(t, dense(X), tc_threshold=0)
-    if kernel == "ldg":
+    if kernel in ("ldg", "tma"):
         want = oracle.bcsr_spmm(oracle.bcsr_from_csr(g), X, tc_threshold=0)
     else:
         want = oracle.csr_spmm(g, oracle.tf32_trunc(X))
