@@ -92,6 +92,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def pull_kernel_name(F):
+    """The BCSR pull kernel the library dispatches for width F (the bulk-copy
+    kernel for F a multiple of 128 unless TCC_PULL_KERNEL picks another)."""
+    choice = os.environ.get("TCC_PULL_KERNEL", "")
+    if choice == "tma" or (choice == "" and F % 128 == 0):
+        return "pull_tma_kernel"
+    if choice == "umma":
+        return "pull_umma_kernel"
+    return "pull_kernel"
+
+
 def profiled_traffic(kernel_tag):
     """dram bytes per launch recorded from an ncu capture in profiles/ (or None)."""
     d = os.path.join(ROOT, "profiles")
@@ -425,8 +436,8 @@ def run_ours(args, rank, world, local_rank):
                    "convert_s": round(W["conv_s"], 3)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": profiled_traffic("pull_kernel_config2") if world == 1 else None,
-                     "kernel": "pull_kernel, forward SpMM" + (" (local + halo tiles and the "
+                     "traffic": profiled_traffic(f"{pull_kernel_name(F)}_config2") if world == 1 else None,
+                     "kernel": f"{pull_kernel_name(F)}, forward SpMM" + (" (local + halo tiles and the "
                                                               "exchange)" if not replicated else
                                                               " (rank 0's rows)" if world > 1 else ""),
                      "fwd_ms": round(fwd_ms, 4), "alg_bytes_per_launch": b_alg,

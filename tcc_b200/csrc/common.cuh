@@ -69,6 +69,9 @@ __device__ __forceinline__ uint32_t f32_to_tf32(float x) {
 // half a TF32 ulp to the magnitude bits and clear the 13 dropped bits.  Same
 // result as the documented cvt.rna mode for finite inputs, without the
 // conversion-unit round trip.
+// Round to TF32 (10 explicit mantissa bits), nearest with ties away from
+// zero: two integer ops, measured faster than cvt.rna.tf32.f32 in the pull
+// kernels.
 __device__ __forceinline__ uint32_t tf32_rna_bits(float x) {
     return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }

@@ -19,7 +19,8 @@ __device__ __forceinline__ float comp(const float4& v, int c) {
 // pass2 == false: one TF32 pass with operands rounded like cvt.rna (the
 // reference's dense-tile arithmetic).  pass2 == true: fp32-accurate split
 // x = hi + lo (hi = x with the low 13 bits cleared, exact), all hi MMAs
-// first, then all lo MMAs.
+// first, then all lo MMAs.  The hi MMAs take the raw fp32 bits: the tensor
+// core ignores the low 13 bits of a TF32 operand, which leaves exactly hi.
 template <int NP>
 __device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 (&x)[2][2 * NP],
                                          uint64_t bm, int gid, int tig, bool pass2) {
@@ -42,13 +43,11 @@ __device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const uint32_t hi[4] = {
-                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
+                __float_as_uint(comp(x[0][2 * p], c)), __float_as_uint(comp(x[0][2 * p + 1], c)),
+                __float_as_uint(comp(x[1][2 * p], c)), __float_as_uint(comp(x[1][2 * p + 1], c))};
             mma_tf32_16x8x8(dacc[4 * p + c], hi, b);
         }
-    // lo = x - hi is exact in fp32; recomputed here to keep registers free
+    // lo = x - hi is exact in fp32
 #pragma unroll
     for (int p = 0; p < NP; ++p)
 #pragma unroll
@@ -60,87 +59,6 @@ __device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 
             for (int e = 0; e < 4; ++e)
                 lo[e] = __float_as_uint(v[e] - __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
             mma_tf32_16x8x8(dacc[4 * p + c], lo, b);
-        }
-}
-
-// tile_mma with the column scale folded into B: B[k][n] = bit(n*8+k) ? c_k : 0,
-// x holds the unscaled rows (zeros for padding rows).  Lane (gid, tig) passes
-// c0 = scale of gather row tig, c1 = of row tig + 4.
-// pass2 == false: one TF32 pass on the raw fp32 bits -- the tensor core drops
-// the low 13 mantissa bits of each operand, the same arithmetic as the
-// tcgen05 kind::tf32 path -- with B split into its TF32 part and remainder
-// when `scaled`, so the column scale keeps fp32 accuracy.
-// pass2 == true: fp32-level split -- a = a_hi + a_lo, b = b_hi + b_lo (hi: low
-// 13 bits cleared, exact in TF32) and D += a_hi*b_hi + a_lo*b_hi (+ a_hi*b_lo
-// when `scaled`; with unit scales b_lo is 0).  The dropped a_lo*b_lo term is
-// below 2^-20 relative.
-template <int NP>
-__device__ __forceinline__ void tile_mma_scaled(float (&dacc)[4 * NP][4],
-                                                const float4 (&x)[2][2 * NP], uint64_t bm,
-                                                float c0, float c1, int gid, int tig, bool pass2,
-                                                bool scaled) {
-    const float bf0 = ((bm >> (gid * 8 + tig)) & 1ull) ? c0 : 0.f;
-    const float bf1 = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? c1 : 0.f;
-    if (!pass2) {
-        const uint32_t b[2] = {__float_as_uint(bf0), __float_as_uint(bf1)};
-#pragma unroll
-        for (int p = 0; p < NP; ++p)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint32_t a[4] = {__float_as_uint(comp(x[0][2 * p], c)), __float_as_uint(comp(x[0][2 * p + 1], c)),
-                                       __float_as_uint(comp(x[1][2 * p], c)), __float_as_uint(comp(x[1][2 * p + 1], c))};
-                mma_tf32_16x8x8(dacc[4 * p + c], a, b);
-            }
-        if (!scaled) return;
-        const uint32_t bl[2] = {__float_as_uint(bf0 - __uint_as_float(__float_as_uint(bf0) & 0xFFFFE000u)),
-                                __float_as_uint(bf1 - __uint_as_float(__float_as_uint(bf1) & 0xFFFFE000u))};
-#pragma unroll
-        for (int p = 0; p < NP; ++p)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint32_t a[4] = {__float_as_uint(comp(x[0][2 * p], c)), __float_as_uint(comp(x[0][2 * p + 1], c)),
-                                       __float_as_uint(comp(x[1][2 * p], c)), __float_as_uint(comp(x[1][2 * p + 1], c))};
-                mma_tf32_16x8x8(dacc[4 * p + c], a, bl);
-            }
-        return;
-    }
-    const uint32_t bh[2] = {__float_as_uint(bf0) & 0xFFFFE000u, __float_as_uint(bf1) & 0xFFFFE000u};
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t hi[4] = {
-                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
-            mma_tf32_16x8x8(dacc[4 * p + c], hi, bh);
-        }
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const float v[4] = {comp(x[0][2 * p], c), comp(x[0][2 * p + 1], c),
-                                comp(x[1][2 * p], c), comp(x[1][2 * p + 1], c)};
-            uint32_t lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                lo[e] = __float_as_uint(v[e] - __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u));
-            mma_tf32_16x8x8(dacc[4 * p + c], lo, bh);
-        }
-    if (!scaled) return;
-    const uint32_t bl[2] = {__float_as_uint(bf0 - __uint_as_float(bh[0])),
-                            __float_as_uint(bf1 - __uint_as_float(bh[1]))};
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t hi[4] = {
-                __float_as_uint(comp(x[0][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[0][2 * p + 1], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p], c)) & 0xFFFFE000u,
-                __float_as_uint(comp(x[1][2 * p + 1], c)) & 0xFFFFE000u};
-            mma_tf32_16x8x8(dacc[4 * p + c], hi, bl);
         }
 }
 

@@ -118,7 +118,8 @@ PULL_KERNELS = ["default", "ldg", "tma", "umma"]
 
 @pytest.fixture(params=PULL_KERNELS)
 def pull_kernel(request, monkeypatch):
-    """Run a pull test on each pull kernel: the default dispatch, the
+    """Run a pull test on each pull kernel: the default dispatch (bulk-copy
+    kernel for F a multiple of 128, register-gather kernel otherwise), the
     register-gather kernel (TCC_PULL_KERNEL=ldg), the bulk-copy gather kernel
     (=tma) and the tcgen05 kernel (=umma; tc_threshold 0, F a multiple of
     128).  Shapes a kernel does not take fall back to the register-gather
