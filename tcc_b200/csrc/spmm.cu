@@ -55,7 +55,7 @@ int grid_sms() {
 namespace {
 
 constexpr uint32_t kChunkTiles = 16;  // max tiles per warp task
-constexpr int kPushWarps = 4;         // warps per push block
+constexpr int kPushWarps = 8;         // warps per push block
 constexpr int kStage = 136;           // floats per staged 128-feature row (bank-conflict free)
 
 struct PlanHeader {
@@ -304,34 +304,107 @@ __global__ void __launch_bounds__(kPullWarps * 32, 2) pull_kernel(PullTiles a, D
 }
 
 // ---------------------------------------------------------------- push ----
+// A window scatters its 8 input rows into the output rows of its tiles.
+// Work split: every warp takes an equal contiguous slice of the tile range
+// and walks the windows that meet it (a window's 8 input rows are reloaded
+// by each warp that meets it), so a hub window with thousands of tiles is
+// shared by many warps instead of setting the kernel's length.  SWTCF: the
+// slices stay inside one super-window (its repeat cache lives in the CTA's
+// shared memory); a super-window with more than kPushPartTiles tiles is
+// split over up to kPushParts CTAs, each of which flushes the cached rows it
+// touched.  Tile arithmetic: TF32 with cvt.rna operands for tiles with
+// popcount >= tc_threshold, the fp32-level hi/lo TF32 split otherwise, both
+// on the window's A fragments built once per window.
+constexpr uint32_t kPushParts = 8;       // most CTAs per SWTCF super-window
+constexpr uint32_t kPushPartTiles = 2048;  // tiles per CTA before a super-window is split
+
+// First w in [lo, hi) with off[w + 1] > t (hi if none); uniform result.
+__device__ __forceinline__ uint32_t warp_first_window(const uint32_t* __restrict__ off, uint32_t lo,
+                                                      uint32_t hi, uint32_t t, int lane) {
+    while (hi - lo > 32) {
+        const uint32_t step = (hi - lo + 31) / 32;
+        const uint32_t q = lo + lane * step;
+        const bool tested = q < hi;
+        const unsigned m = __ballot_sync(0xffffffffu, tested && off[q + 1] > t);
+        if (m == 0) {  // the answer lies past the last tested probe
+            const unsigned tm = __ballot_sync(0xffffffffu, tested);
+            lo += (31 - __clz(tm)) * step + 1;
+        } else {
+            const int k = __ffs(m) - 1;
+            hi = lo + k * step;
+            if (k > 0) lo += (k - 1) * step + 1;
+        }
+    }
+    const uint32_t q = lo + lane;
+    const unsigned m = __ballot_sync(0xffffffffu, q < hi && off[q + 1] > t);
+    return m ? lo + __ffs(m) - 1 : hi;
+}
+
 template <bool SWTCF, bool STORE>
 __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dense d, uint32_t thr,
                                                                FeatureStore fs) {
     __shared__ __align__(16) float stage[kPushWarps * 8 * kStage];
-    __shared__ __align__(16) float cache[SWTCF ? 32 * 128 : 4];
+    extern __shared__ __align__(16) float cache[];  // SWTCF: 32 x 128 repeat-cache rows
+    __shared__ uint32_t touched;  // bit c: repeat-cache row c received a partial sum
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
     const uint32_t f = blockIdx.y * 128 + lane * 4;
     const bool fvalid = f < d.F;
     float* st = stage + wib * 8 * kStage;
     const int gid = lane >> 2, tig = lane & 3;
+    const uint32_t* off = a.win_offset;
 
-    uint32_t w_begin, w_step, s = 0, swoff = 0;
-    uint32_t w_end = a.num_windows;
+    uint32_t s = 0, swoff = 0, wlo = 0, whi = a.num_windows, t0, t1;
     if (SWTCF) {
         s = blockIdx.x;
-        w_begin = s * a.S + wib;
-        w_end = min(a.num_windows, (s + 1) * a.S);
-        w_step = kPushWarps;
+        wlo = s * a.S;
+        whi = min(a.num_windows, wlo + a.S);
+        const uint32_t ta = off[wlo], len = off[whi] - ta;
+        const uint32_t parts = min(kPushParts, max(1u, (len + kPushPartTiles - 1) / kPushPartTiles));
+        if (blockIdx.z >= parts) return;  // uniform over the block, before any barrier
+        const uint64_t pieces = (uint64_t)parts * kPushWarps;
+        const uint64_t piece = (uint64_t)blockIdx.z * kPushWarps + wib;
+        t0 = ta + (uint32_t)(len * piece / pieces);
+        t1 = ta + (uint32_t)(len * (piece + 1) / pieces);
         swoff = a.sw_offset[s];
         for (int e = threadIdx.x; e < 32 * 128; e += blockDim.x) cache[e] = 0.f;
+        if (threadIdx.x == 0) touched = 0;
         __syncthreads();
     } else {
-        w_begin = blockIdx.x * kPushWarps + wib;
-        w_step = gridDim.x * kPushWarps;
+        const uint64_t G = (uint64_t)gridDim.x * kPushWarps;
+        const uint64_t g = (uint64_t)blockIdx.x * kPushWarps + wib;
+        const uint64_t T = off[a.num_windows];
+        t0 = (uint32_t)(T * g / G);
+        t1 = (uint32_t)(T * (g + 1) / G);
     }
 
-    for (uint32_t w = w_begin; w < w_end; w += w_step) {
+    // ---- per-tile metadata, two tiles ahead: bitmap + raw index (t + 2),
+    // output row + repeat-cache slot (t + 1, a dependent load for SWTCF)
+    auto load_raw = [&](uint32_t t, unsigned long long& bm, uint32_t& raw) {
+        bm = 0;
+        raw = kInvalid;
+        if (t < t1) {
+            bm = ld_stream_u64(a.bits + t);
+            if (lane < 8) raw = ld_stream_u32(a.idx + (uint64_t)t * 8 + lane);
+        }
+    };
+    auto resolve = [&](uint32_t raw, uint32_t& orow, uint32_t& cslot) {
+        orow = kInvalid;
+        cslot = 0xFFu;
+        if (SWTCF) {
+            if (raw != kInvalid) {
+                orow = __ldg(a.sw_rows + swoff + raw);
+                cslot = __ldg(a.sw_cache_slot + swoff + raw);
+            }
+        } else {
+            orow = raw < a.num_out ? raw : kInvalid;
+        }
+    };
+
+    // A fragments of the current window: raw fp32 bits (the hi part for the
+    // tensor core, which ignores the low 13 bits) and the exact remainder
+    uint32_t ahi[8][4], alo[8][4];
+    auto load_window = [&](uint32_t w) {
         float4 x[8];
         const float* xp = nullptr;
         if (STORE && lane < 8 && w * 8 + lane < a.num_in) xp = store_row(fs, w * 8 + lane, d.F);
@@ -357,92 +430,111 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
             }
             if (d.cs && cidx < a.num_in) x[k] = f4_scale(x[k], __ldg(d.cs + cidx));
         }
-        bool have_a = false;
-        uint32_t afr[8][4];
-        const uint32_t tb = a.win_offset[w], te = a.win_offset[w + 1];
-        for (uint32_t t = tb; t < te; ++t) {
-            uint64_t bm = ld_stream_u64(a.bits + t);
-            if (a.bits_transposed) bm = transpose8x8(bm);
-            uint32_t orow = kInvalid;
-            uint32_t cslot = 0xFFu;
-            if (lane < 8) {
-                const uint32_t raw = ld_stream_u32(a.idx + (uint64_t)t * 8 + lane);
-                if (SWTCF) {
-                    if (raw != kInvalid) {
-                        orow = __ldg(a.sw_rows + swoff + raw);
-                        cslot = __ldg(a.sw_cache_slot + swoff + raw);
-                    }
-                } else {
-                    orow = raw < a.num_out ? raw : kInvalid;
-                }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) *reinterpret_cast<float4*>(st + k * kStage + lane * 4) = x[k];
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float v[4] = {st[tig * kStage + 16 * j + gid], st[tig * kStage + 16 * j + gid + 8],
+                                st[(tig + 4) * kStage + 16 * j + gid],
+                                st[(tig + 4) * kStage + 16 * j + gid + 8]};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                ahi[j][e] = __float_as_uint(v[e]);
+                alo[j][e] = __float_as_uint(v[e] - __uint_as_float(ahi[j][e] & 0xFFFFE000u));
             }
-            float4 v[8];
+        }
+        __syncwarp();
+    };
+
+    if (t0 < t1) {
+        uint32_t w = warp_first_window(off, wlo, whi, t0, lane);
+        uint32_t wend = off[w + 1];
+        load_window(w);
+        unsigned long long bm0, bm1;
+        uint32_t raw0, raw1, orow0, cslot0;
+        load_raw(t0, bm0, raw0);
+        load_raw(t0 + 1, bm1, raw1);
+        resolve(raw0, orow0, cslot0);
+        for (uint32_t t = t0; t < t1; ++t) {
+            if (t >= wend) {  // uniform: next window that holds tile t
+                do {
+                    ++w;
+                    wend = off[w + 1];
+                } while (wend <= t);
+                load_window(w);
+            }
+            uint32_t orow1, cslot1, raw2;
+            unsigned long long bm2;
+            resolve(raw1, orow1, cslot1);
+            load_raw(t + 2, bm2, raw2);
+
+            unsigned long long bm = bm0;
+            if (a.bits_transposed) bm = transpose8x8(bm);
+            uint32_t b[2];
+            b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
+            b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
+            float dd[8][4];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dd[j][0] = dd[j][1] = dd[j][2] = dd[j][3] = 0.f;
             if ((uint32_t)__popcll(bm) >= thr) {
-                if (!have_a) {
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        *reinterpret_cast<float4*>(st + k * kStage + lane * 4) = x[k];
-                    __syncwarp();
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        afr[j][0] = f32_to_tf32(st[tig * kStage + 16 * j + gid]);
-                        afr[j][1] = f32_to_tf32(st[tig * kStage + 16 * j + gid + 8]);
-                        afr[j][2] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid]);
-                        afr[j][3] = f32_to_tf32(st[(tig + 4) * kStage + 16 * j + gid + 8]);
-                    }
-                    __syncwarp();
-                    have_a = true;
-                }
-                uint32_t b[2];
-                b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
-                b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    float dd[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma_tf32_16x8x8(dd, afr[j], b);
-                    st[(2 * tig) * kStage + 16 * j + gid] = dd[0];
-                    st[(2 * tig + 1) * kStage + 16 * j + gid] = dd[1];
-                    st[(2 * tig) * kStage + 16 * j + gid + 8] = dd[2];
-                    st[(2 * tig + 1) * kStage + 16 * j + gid + 8] = dd[3];
+                    const uint32_t ar[4] = {f32_to_tf32(__uint_as_float(ahi[j][0])),
+                                            f32_to_tf32(__uint_as_float(ahi[j][1])),
+                                            f32_to_tf32(__uint_as_float(ahi[j][2])),
+                                            f32_to_tf32(__uint_as_float(ahi[j][3]))};
+                    mma_tf32_16x8x8(dd[j], ar, b);
                 }
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const float4*>(st + i * kStage + lane * 4);
-                __syncwarp();
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
-                    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int j = 0; j < 8; ++j) mma_tf32_16x8x8(dd[j], ahi[j], b);
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if ((rb >> k) & 1u) v[i] = f4_add(v[i], x[k]);
-                }
+                for (int j = 0; j < 8; ++j) mma_tf32_16x8x8(dd[j], alo[j], b);
             }
+            // D[feature][slot] -> slot-major rows in shared memory
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                st[(2 * tig) * kStage + 16 * j + gid] = dd[j][0];
+                st[(2 * tig + 1) * kStage + 16 * j + gid] = dd[j][1];
+                st[(2 * tig) * kStage + 16 * j + gid + 8] = dd[j][2];
+                st[(2 * tig + 1) * kStage + 16 * j + gid + 8] = dd[j][3];
+            }
+            __syncwarp();
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
-                const uint32_t r = __shfl_sync(0xffffffffu, orow, i);
-                const uint32_t cs = __shfl_sync(0xffffffffu, cslot, i);
+                const uint32_t r = __shfl_sync(0xffffffffu, orow0, i);
+                const uint32_t cs = __shfl_sync(0xffffffffu, cslot0, i);
                 if (rb == 0 || r >= a.num_out || !fvalid) continue;
+                const float4 v = *reinterpret_cast<const float4*>(st + i * kStage + lane * 4);
                 if (SWTCF && cs != 0xFFu) {
                     float* cp = cache + cs * 128 + lane * 4;
-                    atomicAdd(cp + 0, v[i].x);
-                    atomicAdd(cp + 1, v[i].y);
-                    atomicAdd(cp + 2, v[i].z);
-                    atomicAdd(cp + 3, v[i].w);
+                    atomicAdd(cp + 0, v.x);
+                    atomicAdd(cp + 1, v.y);
+                    atomicAdd(cp + 2, v.z);
+                    atomicAdd(cp + 3, v.w);
+                    if (lane == 0) atomicOr(&touched, 1u << cs);
                 } else {
-                    float4 o = v[i];
+                    float4 o = v;
                     if (d.rs) o = f4_scale(o, __ldg(d.rs + r));
                     red_add_v4(d.Y + (uint64_t)r * d.ldy + f, o);
                 }
             }
+            __syncwarp();
+            bm0 = bm1;
+            orow0 = orow1;
+            cslot0 = cslot1;
+            bm1 = bm2;
+            raw1 = raw2;
         }
     }
     if (SWTCF) {
         __syncthreads();
         const uint32_t cc = a.sw_cached_count[s];
+        const uint32_t used = touched;
         for (uint32_t c = wib; c < cc; c += kPushWarps) {
+            if (!((used >> c) & 1u)) continue;
             const uint32_t slot = a.sw_cached_row_slot[(uint64_t)s * 32 + c];
             const uint32_t r = a.sw_rows[swoff + slot];
             if (!fvalid || r >= a.num_out) continue;
@@ -558,7 +650,10 @@ void push_spmm(const PushTiles& a, const Dense& d, uint32_t tc_threshold, const 
     if (a.sw_rows) {
         TCC_REQUIRE(!fs, "the SWTCF pass reads a dense X");
         const uint32_t SW = (a.num_windows + a.S - 1) / a.S;
-        push_kernel<true, false><<<dim3(SW, gy), kPushWarps * 32, 0, s>>>(a, d, tc_threshold, f);
+        auto k = push_kernel<true, false>;
+        constexpr int kCacheBytes = 32 * 128 * sizeof(float);
+        TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kCacheBytes));
+        k<<<dim3(SW, gy, kPushParts), kPushWarps * 32, kCacheBytes, s>>>(a, d, tc_threshold, f);
     } else {
         const unsigned want = ceil_div(a.num_windows, kPushWarps);
         if (fs) {
