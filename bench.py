@@ -450,10 +450,41 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clocks,
     }
     if world == 1:
+        line["swtcf_forward"] = swtcf_forward(W["rowptr"], W["col"], W["n"], X, device)
         g = host_csr(W["rowptr"], W["col"], W["n"])
         s = W["s"].cpu().numpy()
         line["cpu_baseline"] = cpu_baseline(g, X.cpu().numpy(), s, s)
     print(json.dumps(line), flush=True)
+
+
+def swtcf_forward(rowptr, col, n, X, device, reps=5):
+    """Informative: the reference-named SWTCF forward (tcc_swtcf_spmm, the
+    push kernel; pattern-only, F = 128, tc_threshold 12) on the same graph,
+    the call the reference arm times for the reference kernel
+    (reference_gpu_kernel).  Conversion outside the timing; median of reps."""
+    import torch
+    from tcc_b200 import swtcf
+    E = col.numel()
+    m = swtcf.SWTCFMatrix(n, n, E, 16)
+    ws = swtcf.SWTCFConvertWorkspace(E, n, 16)
+    swtcf.convert_csr(rowptr, col, m, ws)
+    ws.free()
+    Y = torch.zeros((n, 128), device=device)
+    swtcf.spmm(m, X, Y, tc_threshold=12)
+    ts = []
+    for _ in range(reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        swtcf.spmm(m, X, Y, tc_threshold=12)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    m.free()
+    ms = statistics.median(ts)
+    return {"what": "tcc_swtcf_spmm (launchSWTCFSpMM's entry point), pattern-only, forward only",
+            "ms": round(ms, 3), "value": round(2.0 * E * 128 / (ms * 1e-3) / 1e9, 2),
+            "unit": "GFLOP/s"}
 
 
 def run_config5(args, rank, world, local_rank):
