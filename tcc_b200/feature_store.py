@@ -53,6 +53,29 @@ class FeatureStore:
         self.gpu_ptrs = torch.tensor([self.gpu_rows.data_ptr()], dtype=torch.int64, device=device)
         self.n_hot, self.n_cold = n_hot, int(cold.size)
 
+    def enable_cold_staging(self, budget_bytes: int | None = None) -> bool:
+        """Allocate an HBM staging buffer for the cold rows if the cold block fits
+        ``budget_bytes`` (default: a quarter of the device's free memory).  The
+        cold rows stay in pinned host memory; ``stage_cold`` streams them into
+        the buffer with one bulk copy (one PCIe crossing per row instead of one
+        per gather that touches it), and an aggregation given ``cold_stage``
+        reads them from HBM.  Returns whether staging is on."""
+        if self.n_cold == 0:
+            return False
+        device = self.gpu_rows.device
+        if budget_bytes is None:
+            free, _ = torch.cuda.mem_get_info(device)
+            budget_bytes = free // 4
+        if self.cold_bytes() > budget_bytes:
+            return False
+        self.cold_stage = torch.empty(self.cpu_rows.shape, dtype=torch.float32, device=device)
+        return True
+
+    def stage_cold(self, stream: torch.cuda.Stream) -> None:
+        """Copy the pinned cold rows into the staging buffer on ``stream`` (async)."""
+        with torch.cuda.stream(stream):
+            self.cold_stage.copy_(self.cpu_rows, non_blocking=True)
+
     @property
     def cpu_ptr(self) -> int:
         """Device-visible address of the pinned host rows (unified addressing)."""

@@ -18,6 +18,12 @@ own rows:
   buffer (DDP's gradient all-reduce, issued explicitly so every rank's
   collectives run in the same order as its halo exchanges), then Adam.
 
+Cold feature rows stay in pinned host memory; each epoch they are streamed
+into an HBM staging buffer by one bulk copy on a side stream, overlapped with
+the previous epoch (``--cold-zero-copy`` gathers them zero-copy instead, one
+PCIe read per gather; the staging buffer is only used when the cold block fits
+a quarter of free HBM).
+
 ``transform_first`` computes layer 2 as Â·(H1·W2) (47 wide instead of 256; the
 reference always aggregates first).  ``--save`` / ``--resume`` write and read a
 checkpoint of the weights, the Adam state and the epoch count (the reference
@@ -44,9 +50,12 @@ from .feature_store import FeatureStore
 from .partition import DistGraph, balanced_bounds, nccl_options
 
 
-def _store_aggregate(tiles_g: T.Tiles, store: FeatureStore, rs: torch.Tensor) -> torch.Tensor:
+def _store_aggregate(tiles_g: T.Tiles, store: FeatureStore, rs: torch.Tensor,
+                     cold: torch.Tensor | None = None) -> torch.Tensor:
     """Â[P_g, :] · X with X read from the store (whose rows carry the column
-    scale); the row scale is applied here."""
+    scale); the row scale is applied here.  ``cold``: the store's HBM staging
+    buffer holding this epoch's copy of the cold rows (None: read them from
+    pinned host memory, zero-copy)."""
     import ctypes as C
     from . import _lib as L
     F = store.F
@@ -54,8 +63,9 @@ def _store_aggregate(tiles_g: T.Tiles, store: FeatureStore, rs: torch.Tensor) ->
     full = torch.empty(((W + 1) * 8, F), dtype=torch.float32, device=rs.device)
     sc = tiles_g.scratch()
     s = tiles_g.struct()
+    cold_ptr = store.cpu_ptr if cold is None else cold.data_ptr()
     L.call("tcc_cnic_forward_mixed", C.byref(s), None, C.c_void_p(store.id_map.data_ptr()),
-           C.c_void_p(store.cpu_ptr), C.c_void_p(store.cache_search_map.data_ptr()),
+           C.c_void_p(cold_ptr), C.c_void_p(store.cache_search_map.data_ptr()),
            C.c_void_p(store.gpu_ptrs.data_ptr()), store.capacity, C.c_void_p(full.data_ptr()), F, 0,
            C.c_void_p(sc.data_ptr()), sc.numel(), C.c_void_p(torch.cuda.current_stream().cuda_stream))
     tiles_g._plan_ready = True
@@ -130,13 +140,32 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool = Fals
             W2.copy_(ck["W2"])
         opt.load_state_dict(ck["opt"])
         start_epoch = int(ck["epoch"])
+    # cold rows: streamed into an HBM staging buffer once per epoch on a side
+    # stream (the copy for epoch e + 1 overlaps the rest of epoch e), or read
+    # zero-copy from pinned host memory by every gather that touches them
+    store = R["store"]
+    staged = bool(cfg.get("cold_staging", True)) and store.enable_cold_staging()
+    if staged:
+        side = torch.cuda.Stream(device=device)
+        ready = torch.cuda.Event()
+        used = torch.cuda.Event()
+        store.stage_cold(side)
+        ready.record(side)
     drop = torch.Generator(device=device)
     drop.manual_seed(cfg["seed"] * 1000 + rank)
     cls_pad = (cfg["classes"] + 3) // 4 * 4  # transform-first SpMM width, multiple of 4
 
     def epoch():
         opt.zero_grad(set_to_none=True)
-        Z1 = _store_aggregate(R["tiles_g"], R["store"], R["rs"])
+        if staged:
+            torch.cuda.current_stream().wait_event(ready)
+            Z1 = _store_aggregate(R["tiles_g"], store, R["rs"], cold=store.cold_stage)
+            used.record()
+            side.wait_event(used)
+            store.stage_cold(side)  # next epoch's copy
+            ready.record(side)
+        else:
+            Z1 = _store_aggregate(R["tiles_g"], store, R["rs"])
         H1 = torch.relu(Z1 @ W1)
         keep = torch.rand(H1.shape, generator=drop, device=device) >= cfg["dropout"]
         H1 = H1 * keep / (1.0 - cfg["dropout"])
@@ -189,7 +218,7 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool = Fals
         dist.all_reduce(halo)
     return dict(epoch_s=t.tolist(), losses=losses, nnz=float(nnz), halo_rows=float(halo),
                 gen_s=R["gen_s"], conv_s=R["conv_s"], store_hot=R["store"].n_hot,
-                store_cold=R["store"].n_cold)
+                store_cold=R["store"].n_cold, cold_staging=staged)
 
 
 CONFIG4 = dict(nodes=2_449_029, edges=61_900_000, seed=3, F_in=100, hidden=256, classes=47,
@@ -208,6 +237,8 @@ def main(argv=None):
     p.add_argument("--shrink", type=int, default=0, help="divide nodes and edges by 2**shrink")
     p.add_argument("--epochs", type=int, default=10)
     p.add_argument("--transform-first", action="store_true")
+    p.add_argument("--cold-zero-copy", action="store_true",
+                   help="read cold rows from pinned host memory in every gather (no HBM staging)")
     p.add_argument("--save", default=None, help="checkpoint path written at the end (rank 0)")
     p.add_argument("--resume", default=None, help="checkpoint to continue from")
     a = p.parse_args(argv)
@@ -223,6 +254,7 @@ def main(argv=None):
         cfg = config(a.shrink)
         cfg["epochs"] = a.epochs
         cfg["save"], cfg["resume"] = a.save, a.resume
+        cfg["cold_staging"] = not a.cold_zero_copy
         r = train(cfg, device, world, rank, a.transform_first)
         if rank == 0:
             steady = r["epoch_s"][1:] or r["epoch_s"]
@@ -234,6 +266,9 @@ def main(argv=None):
                 "config": {"workload": "config4", "nodes": cfg["nodes"], "nnz": int(r["nnz"]),
                            "F_in": cfg["F_in"], "hidden": cfg["hidden"], "classes": cfg["classes"],
                            "hot_rows": r["store_hot"], "cold_rows": r["store_cold"],
+                           "cold_rows_path": ("pinned host -> HBM staging buffer, one bulk copy per "
+                                              "epoch on a side stream (overlapped)" if r["cold_staging"]
+                                              else "zero-copy reads of pinned host memory"),
                            "halo_rows_total": int(r["halo_rows"]), "transform_first": a.transform_first,
                            "order": "layer 1 from the hot/cold store, layer 2 over the row partition"}}),
                   flush=True)

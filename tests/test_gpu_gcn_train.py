@@ -42,13 +42,16 @@ def _dense_loss(cfg, device):
     return float(torch.nn.functional.cross_entropy(logits[idx], y, reduction="sum") / labeled.sum())
 
 
-@pytest.mark.parametrize("transform_first", [False, True])
-def test_gcn_trainer_matches_dense_reference(gpu, transform_first):
+@pytest.mark.parametrize("transform_first,cold_staging", [(False, True), (True, True), (False, False)])
+def test_gcn_trainer_matches_dense_reference(gpu, transform_first, cold_staging):
+    """Cold rows through the HBM staging buffer (default) and zero-copy."""
     cfg = train_gcn.config(shrink=10)
     cfg["dropout"] = 0.0
     cfg["epochs"] = 6
+    cfg["cold_staging"] = cold_staging
     dev = torch.device("cuda", 0)
     r = train_gcn.train(cfg, dev, 1, 0, transform_first=transform_first)
+    assert r["cold_staging"] == cold_staging
     want = _dense_loss(cfg, dev)
     assert abs(r["losses"][0] - want) / want <= 2e-3, (r["losses"][0], want)
     assert r["losses"][-1] < r["losses"][0]
