@@ -71,8 +71,9 @@ def parse():
                    help="spmm: the config-2 SpMM step (headline, weak scaling); gcn4: config-4 GCN "
                         "epoch time (tcc_b200.train_gcn, epochs = --steps); config5: the scale-26 "
                         "forward SpMM, strong scaling")
-    p.add_argument("--transform-first", action="store_true",
-                   help="gcn4: compute layer 2 as A.(H.W) instead of (A.H).W")
+    p.add_argument("--aggregate-first", action="store_true",
+                   help="gcn4: compute layer 2 as (A.H).W, the reference's order, instead of "
+                        "choosing by width (A.(H.W) for 256 -> 47)")
     p.add_argument("--scale5", type=int, default=26, help="config5: R-MAT scale (26 = config 5)")
     p.add_argument("--c5-mode", choices=["exchange", "replicated"], default="exchange",
                    help="config5 on N > 1 GPUs: exchange the X halo every step, or all-gather X "
@@ -692,7 +693,7 @@ def main():
             return
         from tcc_b200 import train_gcn
         train_gcn.main(["--epochs", str(max(args.steps, 2))] +
-                       (["--transform-first"] if args.transform_first else []))
+                       (["--aggregate-first"] if args.aggregate_first else []))
         return
     pg = False
     if world > 1 and args.impl == "ours":

@@ -24,8 +24,11 @@ the previous epoch (``--cold-zero-copy`` gathers them zero-copy instead, one
 PCIe read per gather; the staging buffer is only used when the cold block fits
 a quarter of free HBM).
 
-``transform_first`` computes layer 2 as Â·(H1·W2) (47 wide instead of 256; the
-reference always aggregates first).  ``--save`` / ``--resume`` write and read a
+Layer order by width: a layer aggregates at the narrower of its input and
+output widths.  Layer 1 (100 -> 256) aggregates first; layer 2 (256 -> 47)
+transforms first, Â·(H1·W2), so both of its SpMMs run 48 wide instead of 256
+(``transform_first``; None picks by width, ``--aggregate-first`` keeps the
+reference's order for every layer).  ``--save`` / ``--resume`` write and read a
 checkpoint of the weights, the Adam state and the epoch count (the reference
 saves none).
 
@@ -121,7 +124,9 @@ def build(cfg: dict, device, world: int, rank: int):
                 nnz=int(lcol.numel()), gen_s=gen_s, conv_s=conv_s)
 
 
-def train(cfg: dict, device, world: int, rank: int, transform_first: bool = False):
+def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None = None):
+    if transform_first is None:  # aggregate at the narrower width of layer 2
+        transform_first = cfg["classes"] < cfg["hidden"]
     R = build(cfg, device, world, rank)
     torch.manual_seed(cfg["seed"])
     W1 = torch.empty(cfg["F_in"], cfg["hidden"], device=device)
@@ -218,7 +223,7 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool = Fals
         dist.all_reduce(halo)
     return dict(epoch_s=t.tolist(), losses=losses, nnz=float(nnz), halo_rows=float(halo),
                 gen_s=R["gen_s"], conv_s=R["conv_s"], store_hot=R["store"].n_hot,
-                store_cold=R["store"].n_cold, cold_staging=staged)
+                store_cold=R["store"].n_cold, cold_staging=staged, transform_first=transform_first)
 
 
 CONFIG4 = dict(nodes=2_449_029, edges=61_900_000, seed=3, F_in=100, hidden=256, classes=47,
@@ -236,7 +241,11 @@ def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("--shrink", type=int, default=0, help="divide nodes and edges by 2**shrink")
     p.add_argument("--epochs", type=int, default=10)
-    p.add_argument("--transform-first", action="store_true")
+    order = p.add_mutually_exclusive_group()
+    order.add_argument("--transform-first", dest="order", action="store_const", const="transform",
+                       help="layer 2 as A.(H.W) (the default for these widths)")
+    order.add_argument("--aggregate-first", dest="order", action="store_const", const="aggregate",
+                       help="layer 2 as (A.H).W, the reference's order")
     p.add_argument("--cold-zero-copy", action="store_true",
                    help="read cold rows from pinned host memory in every gather (no HBM staging)")
     p.add_argument("--save", default=None, help="checkpoint path written at the end (rank 0)")
@@ -255,7 +264,8 @@ def main(argv=None):
         cfg["epochs"] = a.epochs
         cfg["save"], cfg["resume"] = a.save, a.resume
         cfg["cold_staging"] = not a.cold_zero_copy
-        r = train(cfg, device, world, rank, a.transform_first)
+        tf = {"transform": True, "aggregate": False}.get(a.order)
+        r = train(cfg, device, world, rank, tf)
         if rank == 0:
             steady = r["epoch_s"][1:] or r["epoch_s"]
             print(json.dumps({
@@ -269,7 +279,7 @@ def main(argv=None):
                            "cold_rows_path": ("pinned host -> HBM staging buffer, one bulk copy per "
                                               "epoch on a side stream (overlapped)" if r["cold_staging"]
                                               else "zero-copy reads of pinned host memory"),
-                           "halo_rows_total": int(r["halo_rows"]), "transform_first": a.transform_first,
+                           "halo_rows_total": int(r["halo_rows"]), "transform_first": r["transform_first"],
                            "order": "layer 1 from the hot/cold store, layer 2 over the row partition"}}),
                   flush=True)
     finally:
