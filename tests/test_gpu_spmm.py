@@ -242,3 +242,37 @@ def test_swtcf_spmm_quantized(gpu, oracle, name, g, thr):
         dst, src = g.coo()
         ref = oracle.ref_swtcf_spmm_quantized(g.rows, g.cols, dst, src, q, scales, src_global, thr)
         assert rel_inf(got, ref) <= REF_TOL, name
+
+
+@pytest.mark.parametrize("thr", [65, 12])
+def test_push_heavy_hub_window(gpu, oracle, thr):
+    """A 40,000-node star: the hub's column window holds ~5,000 tiles, so the
+    push pass shares it among many warps and splits its super-window over
+    several CTAs (each flushing the repeat-cache rows it touched).  SWTCF
+    forward (reference semantics: Y accumulates) and the BCSC push against
+    the oracle, and against the reference kernel where it is built."""
+    n = 40000
+    u = np.zeros(n - 1, np.uint32)
+    v = np.arange(1, n, dtype=np.uint32)
+    g = G._symmetrise_with_loops(u, v, n)
+    X = G.features(g.cols, 128, seed=31)
+    Y0 = G.features(g.rows, 128, seed=32)
+    want = oracle.csr_spmm(g, X) + Y0
+    tol = FP32_TOL if thr > 64 else TF32_TOL
+    m = make_swtcf(g)
+    Yd = dense(Y0)
+    swtcf.spmm(m, dense(X), Yd, tc_threshold=thr)
+    assert rel_fro(Yd.cpu().numpy(), want) <= tol
+    rp, col = csr_dev(g)
+    t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsc")
+    Cd = dense(Y0)
+    tiles.bcsc_spmm(t, dense(X), Cd, tc_threshold=thr)
+    assert rel_fro(Cd.cpu().numpy(), want) <= tol
+    if thr == 12:
+        if oracle.ref_lib() is None:
+            pytest.fail("oracle/_ref/libtcc_ref.so missing: run `make -C oracle ref` before shipping")
+        dst, src = g.coo()
+        ref, _ = oracle.ref_swtcf_spmm(g.rows, g.cols, dst, src, X, tc_threshold=12)
+        Yz = torch.zeros((g.rows, 128), device="cuda")
+        swtcf.spmm(m, dense(X), Yz, tc_threshold=12)
+        assert rel_inf(Yz.cpu().numpy(), ref) <= REF_TOL
