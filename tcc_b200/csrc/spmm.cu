@@ -56,7 +56,6 @@ namespace {
 
 constexpr uint32_t kChunkTiles = 16;  // max tiles per warp task
 constexpr int kPushWarps = 8;         // warps per push block
-constexpr int kStage = 136;           // floats per staged 128-feature row (bank-conflict free)
 
 struct PlanHeader {
     uint32_t num_chunks;
@@ -311,10 +310,11 @@ __global__ void __launch_bounds__(kPullWarps * 32, 2) pull_kernel(PullTiles a, D
 // shared by many warps instead of setting the kernel's length.  SWTCF: the
 // slices stay inside one super-window (its repeat cache lives in the CTA's
 // shared memory); a super-window with more than kPushPartTiles tiles is
-// split over up to kPushParts CTAs, each of which flushes the cached rows it
-// touched.  Tile arithmetic: TF32 with cvt.rna operands for tiles with
-// popcount >= tc_threshold, the fp32-level hi/lo TF32 split otherwise, both
-// on the window's A fragments built once per window.
+// split over up to kPushParts CTAs (adjacent blocks), each of which flushes the
+// cached rows it touched.  Tile arithmetic (push_tile_mma): TF32 with rna
+// operands for tiles with popcount >= tc_threshold, the fp32-level hi/lo TF32
+// split otherwise, on the window's rows held in registers in fragment order;
+// the partial sums are reduced straight from the MMA accumulators.
 constexpr uint32_t kPushParts = 8;       // most CTAs per SWTCF super-window
 constexpr uint32_t kPushPartTiles = 2048;  // tiles per CTA before a super-window is split
 
@@ -340,30 +340,81 @@ __device__ __forceinline__ uint32_t warp_first_window(const uint32_t* __restrict
     return m ? lo + __ffs(m) - 1 : hi;
 }
 
+// One tile of the push pass: D[128 features x 8 output slots] = X_window . B,
+// B[k][n] = bit(n*8 + k), in the permuted fragment order of tile_mma (lane
+// (gid, tig) ends up holding 4 consecutive features of output slots 2tig and
+// 2tig+1).  The window's rows arrive scaled (xr) with their exact remainders
+// below TF32 (xl), both built once per window.  dense: TF32 with cvt.rna
+// operands (the reference's dense-tile arithmetic); otherwise the hi/lo
+// split, whose hi MMAs take the raw fp32 bits.
+__device__ __forceinline__ void push_tile_mma(float (&dacc)[8][4], const float4 (&xr)[2][4],
+                                              const float4 (&xl)[2][4], uint64_t bm, int gid,
+                                              int tig, bool dense) {
+    uint32_t b[2];
+    b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
+    b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
+    if (dense) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t av[4] = {tf32_rna_bits(comp(xr[0][2 * p], c)),
+                                        tf32_rna_bits(comp(xr[0][2 * p + 1], c)),
+                                        tf32_rna_bits(comp(xr[1][2 * p], c)),
+                                        tf32_rna_bits(comp(xr[1][2 * p + 1], c))};
+                mma_tf32_16x8x8(dacc[4 * p + c], av, b);
+            }
+        return;
+    }
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t hi[4] = {__float_as_uint(comp(xr[0][2 * p], c)),
+                                    __float_as_uint(comp(xr[0][2 * p + 1], c)),
+                                    __float_as_uint(comp(xr[1][2 * p], c)),
+                                    __float_as_uint(comp(xr[1][2 * p + 1], c))};
+            mma_tf32_16x8x8(dacc[4 * p + c], hi, b);
+        }
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t lo[4] = {__float_as_uint(comp(xl[0][2 * p], c)),
+                                    __float_as_uint(comp(xl[0][2 * p + 1], c)),
+                                    __float_as_uint(comp(xl[1][2 * p], c)),
+                                    __float_as_uint(comp(xl[1][2 * p + 1], c))};
+            mma_tf32_16x8x8(dacc[4 * p + c], lo, b);
+        }
+}
+
+__device__ __forceinline__ float4 f4_lo(float4 v) {  // v minus its TF32 truncation, exact
+    auto one = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
+    return make_float4(one(v.x), one(v.y), one(v.z), one(v.w));
+}
+
 template <bool SWTCF, bool STORE>
-__global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dense d, uint32_t thr,
-                                                               FeatureStore fs) {
-    __shared__ __align__(16) float stage[kPushWarps * 8 * kStage];
+__global__ void __launch_bounds__(kPushWarps * 32, 2) push_kernel(PushTiles a, Dense d,
+                                                                  uint32_t thr, FeatureStore fs) {
     extern __shared__ __align__(16) float cache[];  // SWTCF: 32 x 128 repeat-cache rows
     __shared__ uint32_t touched;  // bit c: repeat-cache row c received a partial sum
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
-    const uint32_t f = blockIdx.y * 128 + lane * 4;
-    const bool fvalid = f < d.F;
-    float* st = stage + wib * 8 * kStage;
     const int gid = lane >> 2, tig = lane & 3;
+    const uint32_t fb = blockIdx.y * 128;
     const uint32_t* off = a.win_offset;
 
     uint32_t s = 0, swoff = 0, wlo = 0, whi = a.num_windows, t0, t1;
     if (SWTCF) {
-        s = blockIdx.x;
+        s = blockIdx.x / kPushParts;  // a super-window's parts are adjacent blocks
+        const uint32_t part = blockIdx.x % kPushParts;
         wlo = s * a.S;
         whi = min(a.num_windows, wlo + a.S);
         const uint32_t ta = off[wlo], len = off[whi] - ta;
         const uint32_t parts = min(kPushParts, max(1u, (len + kPushPartTiles - 1) / kPushPartTiles));
-        if (blockIdx.z >= parts) return;  // uniform over the block, before any barrier
+        if (part >= parts) return;  // uniform over the block, before any barrier
         const uint64_t pieces = (uint64_t)parts * kPushWarps;
-        const uint64_t piece = (uint64_t)blockIdx.z * kPushWarps + wib;
+        const uint64_t piece = (uint64_t)part * kPushWarps + wib;
         t0 = ta + (uint32_t)(len * piece / pieces);
         t1 = ta + (uint32_t)(len * (piece + 1) / pieces);
         swoff = a.sw_offset[s];
@@ -378,8 +429,9 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
         t1 = (uint32_t)(T * (g + 1) / G);
     }
 
-    // ---- per-tile metadata, two tiles ahead: bitmap + raw index (t + 2),
-    // output row + repeat-cache slot (t + 1, a dependent load for SWTCF)
+    // ---- per-tile metadata, two tiles ahead: bitmap + raw index (t + 2);
+    // output row, repeat-cache slot and row scale (t + 1; dependent loads).
+    // Lane n < 8 holds output slot n.
     auto load_raw = [&](uint32_t t, unsigned long long& bm, uint32_t& raw) {
         bm = 0;
         raw = kInvalid;
@@ -388,7 +440,7 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
             if (lane < 8) raw = ld_stream_u32(a.idx + (uint64_t)t * 8 + lane);
         }
     };
-    auto resolve = [&](uint32_t raw, uint32_t& orow, uint32_t& cslot) {
+    auto resolve = [&](uint32_t raw, uint32_t& orow, uint32_t& cslot, float& rsc) {
         orow = kInvalid;
         cslot = 0xFFu;
         if (SWTCF) {
@@ -399,52 +451,51 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
         } else {
             orow = raw < a.num_out ? raw : kInvalid;
         }
+        rsc = (d.rs && orow < a.num_out) ? __ldg(d.rs + orow) : 1.f;
     };
 
-    // A fragments of the current window: raw fp32 bits (the hi part for the
-    // tensor core, which ignores the low 13 bits) and the exact remainder
-    uint32_t ahi[8][4], alo[8][4];
+    // the window's 8 input rows in fragment order: lane holds rows k = tig + 4r
+    // at features fb + 4*(gid + 8*sl), scaled by the column scale
+    float4 xr[2][4], xl[2][4];
     auto load_window = [&](uint32_t w) {
-        float4 x[8];
         const float* xp = nullptr;
         if (STORE && lane < 8 && w * 8 + lane < a.num_in) xp = store_row(fs, w * 8 + lane, d.F);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int r = 0; r < 2; ++r) {
+            const int k = tig + 4 * r;
             const uint32_t cidx = w * 8 + k;
-            x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (STORE) {
-                const unsigned long long pv =
-                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(xp), k);
-                if (cidx < a.num_in && fvalid)
-                    x[k] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pv) + f);
-            } else if (d.qX) {
-                if (cidx < a.num_in && fvalid) {
-                    // dequantize like the reference: float(q) * scale[g] in fp32
-                    const uint32_t g = d.qmap ? __ldg(d.qmap + cidx) : cidx;
-                    const char4 q = __ldg(reinterpret_cast<const char4*>(d.qX + (uint64_t)g * d.ldq + f));
-                    const float sc = __ldg(d.qscale + g);
-                    x[k] = make_float4((float)q.x * sc, (float)q.y * sc, (float)q.z * sc, (float)q.w * sc);
+            const bool ok = cidx < a.num_in;
+            const float* rowp = nullptr;
+            if (STORE)
+                rowp = reinterpret_cast<const float*>(
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(xp), k));
+            uint32_t g = cidx;
+            float qs = 1.f;
+            if (!STORE && d.qX && ok) {
+                g = d.qmap ? __ldg(d.qmap + cidx) : cidx;
+                qs = __ldg(d.qscale + g);
+            }
+            const float sc = (ok && d.cs) ? __ldg(d.cs + cidx) : 1.f;
+#pragma unroll
+            for (int sl = 0; sl < 4; ++sl) {
+                const uint32_t f = fb + 4 * (gid + 8 * sl);
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ok && f < d.F) {
+                    if (STORE) {
+                        v = *reinterpret_cast<const float4*>(rowp + f);
+                    } else if (d.qX) {
+                        // dequantize like the reference: float(q) * scale[g] in fp32
+                        const char4 q = __ldg(reinterpret_cast<const char4*>(d.qX + (uint64_t)g * d.ldq + f));
+                        v = make_float4((float)q.x * qs, (float)q.y * qs, (float)q.z * qs, (float)q.w * qs);
+                    } else {
+                        v = ld4(d.X + (uint64_t)cidx * d.ldx + f);
+                    }
                 }
-            } else if (cidx < a.num_in && fvalid) {
-                x[k] = ld4(d.X + (uint64_t)cidx * d.ldx + f);
-            }
-            if (d.cs && cidx < a.num_in) x[k] = f4_scale(x[k], __ldg(d.cs + cidx));
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) *reinterpret_cast<float4*>(st + k * kStage + lane * 4) = x[k];
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float v[4] = {st[tig * kStage + 16 * j + gid], st[tig * kStage + 16 * j + gid + 8],
-                                st[(tig + 4) * kStage + 16 * j + gid],
-                                st[(tig + 4) * kStage + 16 * j + gid + 8]};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                ahi[j][e] = __float_as_uint(v[e]);
-                alo[j][e] = __float_as_uint(v[e] - __uint_as_float(ahi[j][e] & 0xFFFFE000u));
+                if (d.cs) v = f4_scale(v, sc);
+                xr[r][sl] = v;
+                xl[r][sl] = f4_lo(v);
             }
         }
-        __syncwarp();
     };
 
     if (t0 < t1) {
@@ -453,9 +504,10 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
         load_window(w);
         unsigned long long bm0, bm1;
         uint32_t raw0, raw1, orow0, cslot0;
+        float rsc0;
         load_raw(t0, bm0, raw0);
         load_raw(t0 + 1, bm1, raw1);
-        resolve(raw0, orow0, cslot0);
+        resolve(raw0, orow0, cslot0, rsc0);
         for (uint32_t t = t0; t < t1; ++t) {
             if (t >= wend) {  // uniform: next window that holds tile t
                 do {
@@ -465,66 +517,55 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
                 load_window(w);
             }
             uint32_t orow1, cslot1, raw2;
+            float rsc1;
             unsigned long long bm2;
-            resolve(raw1, orow1, cslot1);
+            resolve(raw1, orow1, cslot1, rsc1);
             load_raw(t + 2, bm2, raw2);
 
             unsigned long long bm = bm0;
             if (a.bits_transposed) bm = transpose8x8(bm);
-            uint32_t b[2];
-            b[0] = ((bm >> (gid * 8 + tig)) & 1ull) ? kOne : 0u;
-            b[1] = ((bm >> (gid * 8 + tig + 4)) & 1ull) ? kOne : 0u;
-            float dd[8][4];
+            float dacc[8][4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) dd[j][0] = dd[j][1] = dd[j][2] = dd[j][3] = 0.f;
-            if ((uint32_t)__popcll(bm) >= thr) {
+            for (int j = 0; j < 8; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
+            push_tile_mma(dacc, xr, xl, bm, gid, tig, (uint32_t)__popcll(bm) >= thr);
+            // lane (gid, tig) reduces output slots 2tig, 2tig+1 at features
+            // fb + 4*(gid + 8*sl): 8 lanes x 4 float4 cover one 128-feature row
+            uint32_t r[2], cs[2];
+            float rsc[2];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t ar[4] = {f32_to_tf32(__uint_as_float(ahi[j][0])),
-                                            f32_to_tf32(__uint_as_float(ahi[j][1])),
-                                            f32_to_tf32(__uint_as_float(ahi[j][2])),
-                                            f32_to_tf32(__uint_as_float(ahi[j][3]))};
-                    mma_tf32_16x8x8(dd[j], ar, b);
+            for (int h = 0; h < 2; ++h) {
+                r[h] = __shfl_sync(0xffffffffu, orow0, 2 * tig + h);
+                cs[h] = __shfl_sync(0xffffffffu, cslot0, 2 * tig + h);
+                rsc[h] = __shfl_sync(0xffffffffu, rsc0, 2 * tig + h);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int slot = 2 * tig + h;
+                if (((bm >> (8 * slot)) & 0xFFull) == 0 || r[h] >= a.num_out) continue;
+                const bool cached = SWTCF && cs[h] != 0xFFu;
+#pragma unroll
+                for (int sl = 0; sl < 4; ++sl) {
+                    const uint32_t f = fb + 4 * (gid + 8 * sl);
+                    if (f >= d.F) continue;
+                    const int p = sl >> 1, e = (sl & 1) * 2 + h;
+                    float4 v = make_float4(dacc[4 * p + 0][e], dacc[4 * p + 1][e],
+                                           dacc[4 * p + 2][e], dacc[4 * p + 3][e]);
+                    if (cached) {
+                        float* cp = cache + cs[h] * 128 + (f - fb);
+                        atomicAdd(cp + 0, v.x);
+                        atomicAdd(cp + 1, v.y);
+                        atomicAdd(cp + 2, v.z);
+                        atomicAdd(cp + 3, v.w);
+                    } else {
+                        red_add_v4(d.Y + (uint64_t)r[h] * d.ldy + f, f4_scale(v, rsc[h]));
+                    }
                 }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) mma_tf32_16x8x8(dd[j], ahi[j], b);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) mma_tf32_16x8x8(dd[j], alo[j], b);
+                if (cached && gid == 0) atomicOr(&touched, 1u << cs[h]);
             }
-            // D[feature][slot] -> slot-major rows in shared memory
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                st[(2 * tig) * kStage + 16 * j + gid] = dd[j][0];
-                st[(2 * tig + 1) * kStage + 16 * j + gid] = dd[j][1];
-                st[(2 * tig) * kStage + 16 * j + gid + 8] = dd[j][2];
-                st[(2 * tig + 1) * kStage + 16 * j + gid + 8] = dd[j][3];
-            }
-            __syncwarp();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t rb = (uint32_t)(bm >> (8 * i)) & 0xFFu;
-                const uint32_t r = __shfl_sync(0xffffffffu, orow0, i);
-                const uint32_t cs = __shfl_sync(0xffffffffu, cslot0, i);
-                if (rb == 0 || r >= a.num_out || !fvalid) continue;
-                const float4 v = *reinterpret_cast<const float4*>(st + i * kStage + lane * 4);
-                if (SWTCF && cs != 0xFFu) {
-                    float* cp = cache + cs * 128 + lane * 4;
-                    atomicAdd(cp + 0, v.x);
-                    atomicAdd(cp + 1, v.y);
-                    atomicAdd(cp + 2, v.z);
-                    atomicAdd(cp + 3, v.w);
-                    if (lane == 0) atomicOr(&touched, 1u << cs);
-                } else {
-                    float4 o = v;
-                    if (d.rs) o = f4_scale(o, __ldg(d.rs + r));
-                    red_add_v4(d.Y + (uint64_t)r * d.ldy + f, o);
-                }
-            }
-            __syncwarp();
             bm0 = bm1;
             orow0 = orow1;
             cslot0 = cslot1;
+            rsc0 = rsc1;
             bm1 = bm2;
             raw1 = raw2;
         }
@@ -533,14 +574,15 @@ __global__ void __launch_bounds__(kPushWarps * 32) push_kernel(PushTiles a, Dens
         __syncthreads();
         const uint32_t cc = a.sw_cached_count[s];
         const uint32_t used = touched;
+        const uint32_t f = fb + lane * 4;
         for (uint32_t c = wib; c < cc; c += kPushWarps) {
             if (!((used >> c) & 1u)) continue;
             const uint32_t slot = a.sw_cached_row_slot[(uint64_t)s * 32 + c];
-            const uint32_t r = a.sw_rows[swoff + slot];
-            if (!fvalid || r >= a.num_out) continue;
+            const uint32_t row = a.sw_rows[swoff + slot];
+            if (f >= d.F || row >= a.num_out) continue;
             float4 o = *reinterpret_cast<const float4*>(cache + c * 128 + lane * 4);
-            if (d.rs) o = f4_scale(o, __ldg(d.rs + r));
-            red_add_v4(d.Y + (uint64_t)r * d.ldy + f, o);
+            if (d.rs) o = f4_scale(o, __ldg(d.rs + row));
+            red_add_v4(d.Y + (uint64_t)row * d.ldy + f, o);
         }
     }
 }
@@ -653,7 +695,7 @@ void push_spmm(const PushTiles& a, const Dense& d, uint32_t tc_threshold, const 
         auto k = push_kernel<true, false>;
         constexpr int kCacheBytes = 32 * 128 * sizeof(float);
         TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kCacheBytes));
-        k<<<dim3(SW, gy, kPushParts), kPushWarps * 32, kCacheBytes, s>>>(a, d, tc_threshold, f);
+        k<<<dim3(SW * kPushParts, gy), kPushWarps * 32, kCacheBytes, s>>>(a, d, tc_threshold, f);
     } else {
         const unsigned want = ceil_div(a.num_windows, kPushWarps);
         if (fs) {
