@@ -78,9 +78,10 @@ def parse():
     p.add_argument("--c5-mode", choices=["exchange", "replicated"], default="exchange",
                    help="config5 on N > 1 GPUs: exchange the X halo every step, or all-gather X "
                         "once at set-up (static input features) and run without communication")
-    p.add_argument("--profile", choices=["fwd", "bwd"], default=None,
-                   help="build the workload, run only the forward (or transposed) pull "
-                        "--steps times and exit: the command ncu captures")
+    p.add_argument("--profile", choices=["fwd", "bwd", "swtcf"], default=None,
+                   help="build the workload, run only the forward (or transposed) pull, or the "
+                        "reference-named SWTCF forward (push), --steps times and exit: the "
+                        "command ncu captures")
     return p.parse_args()
 
 
@@ -617,6 +618,19 @@ def run_profile(args):
     import torch
     device = torch.device("cuda", 0)
     W = build_workload(args.scale, device, tc_threshold=args.tc_threshold)
+    if args.profile == "swtcf":
+        from tcc_b200 import swtcf
+        rowptr, col, n = W["full_rowptr"], W["full_col"], W["n"]
+        m = swtcf.SWTCFMatrix(n, n, col.numel(), 16)
+        ws = swtcf.SWTCFConvertWorkspace(col.numel(), n, 16)
+        swtcf.convert_csr(rowptr, col, m, ws)
+        ws.free()
+        Y = torch.zeros((n, 128), device=device)
+        for _ in range(args.steps):
+            swtcf.spmm(m, W["X"], Y, tc_threshold=12)
+        torch.cuda.synchronize()
+        print(f"profile swtcf: {args.steps} launches done", flush=True)
+        return
     dg = W["dg"]
     src = W["X"] if args.profile == "fwd" else W["G"]
     out = torch.empty_like(src)
