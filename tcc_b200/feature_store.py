@@ -53,28 +53,61 @@ class FeatureStore:
         self.gpu_ptrs = torch.tensor([self.gpu_rows.data_ptr()], dtype=torch.int64, device=device)
         self.n_hot, self.n_cold = n_hot, int(cold.size)
 
-    def enable_cold_staging(self, budget_bytes: int | None = None) -> bool:
-        """Allocate an HBM staging buffer for the cold rows if the cold block fits
-        ``budget_bytes`` (default: a quarter of the device's free memory).  The
-        cold rows stay in pinned host memory; ``stage_cold`` streams them into
-        the buffer with one bulk copy (one PCIe crossing per row instead of one
-        per gather that touches it), and an aggregation given ``cold_stage``
-        reads them from HBM.  Returns whether staging is on."""
+    def enable_cold_staging(self, budget_bytes: int | None = None, columns: torch.Tensor | None = None,
+                            force_gather: bool = False) -> bool:
+        """Allocate an HBM staging buffer for the cold rows an aggregation reads,
+        if they fit ``budget_bytes`` (default: a quarter of the device's free
+        memory).  ``columns``: the column ids the aggregation gathers (e.g. a
+        rank's tile indices; out-of-range ids are padding); only the cold rows
+        among them are staged.  The cold rows stay in pinned host memory;
+        ``stage_cold`` brings them over PCIe once per call (one crossing per
+        row instead of one per gather that touches it) and an aggregation reads
+        ``cold_stage`` through ``stage_id_map``.  ``force_gather`` stages through
+        the row-gather kernel even when every cold row is needed (tests).
+        Returns whether staging is on."""
         if self.n_cold == 0:
             return False
         device = self.gpu_rows.device
+        ids = None
+        if columns is not None:
+            c = torch.unique(columns.to(device=device, dtype=torch.int64))
+            c = c[(c >= 0) & (c < self.num_nodes)]
+            c = c[self.cache_search_map[c] < 0]
+            if c.numel() < self.n_cold or force_gather:
+                ids = self.id_map[c].to(torch.int64)
+        n_stage = self.n_cold if ids is None else ids.numel()
         if budget_bytes is None:
             free, _ = torch.cuda.mem_get_info(device)
             budget_bytes = free // 4
-        if self.cold_bytes() > budget_bytes:
+        if n_stage * self.F * 4 > budget_bytes:
             return False
-        self.cold_stage = torch.empty(self.cpu_rows.shape, dtype=torch.float32, device=device)
+        self.cold_stage = torch.empty((max(n_stage, 1), self.F), dtype=torch.float32, device=device)
+        if ids is None:  # every cold row: one bulk copy, same row order as the host block
+            self.stage_ids = None
+            self.stage_id_map = self.id_map
+        else:
+            self.stage_ids = ids
+            stage_map = torch.full((self.num_nodes,), -1, dtype=torch.int32, device=device)
+            stage_map[c] = torch.arange(c.numel(), dtype=torch.int32, device=device)
+            self.stage_id_map = stage_map
         return True
 
     def stage_cold(self, stream: torch.cuda.Stream) -> None:
-        """Copy the pinned cold rows into the staging buffer on ``stream`` (async)."""
-        with torch.cuda.stream(stream):
-            self.cold_stage.copy_(self.cpu_rows, non_blocking=True)
+        """Bring the staged cold rows from pinned host memory into ``cold_stage``
+        on ``stream`` (async): one bulk copy when every cold row is staged, else
+        the row-gather kernel reading the host rows zero-copy."""
+        if self.stage_ids is None:
+            with torch.cuda.stream(stream):
+                self.cold_stage.copy_(self.cpu_rows, non_blocking=True)
+            return
+        if self.stage_ids.numel() == 0:
+            return
+        import ctypes as C
+        from . import _lib as L
+        L.call("tcc_gather_rows", C.c_void_p(self.cpu_rows.data_ptr()), self.F, self.n_cold,
+               C.c_void_p(self.stage_ids.data_ptr()), self.stage_ids.numel(),
+               C.c_void_p(self.cold_stage.data_ptr()), self.F, self.F, None,
+               C.c_void_p(stream.cuda_stream))
 
     @property
     def cpu_ptr(self) -> int:

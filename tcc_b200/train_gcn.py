@@ -18,11 +18,12 @@ own rows:
   buffer (DDP's gradient all-reduce, issued explicitly so every rank's
   collectives run in the same order as its halo exchanges), then Adam.
 
-Cold feature rows stay in pinned host memory; each epoch they are streamed
-into an HBM staging buffer by one bulk copy on a side stream, overlapped with
-the previous epoch (``--cold-zero-copy`` gathers them zero-copy instead, one
-PCIe read per gather; the staging buffer is only used when the cold block fits
-a quarter of free HBM).
+Cold feature rows stay in pinned host memory; each epoch the ones this rank's
+tiles read are brought into an HBM staging buffer on a side stream, overlapped
+with the previous epoch: one bulk copy when the rank reads every cold row, the
+row-gather kernel otherwise (``--cold-zero-copy`` reads them zero-copy in every
+gather instead, one PCIe read per gather; staging is only used when the staged
+rows fit a quarter of free HBM).
 
 Layer order by width: a layer aggregates at the narrower of its input and
 output widths.  Layer 1 (100 -> 256) aggregates first; layer 2 (256 -> 47)
@@ -54,11 +55,11 @@ from .partition import DistGraph, balanced_bounds, nccl_options
 
 
 def _store_aggregate(tiles_g: T.Tiles, store: FeatureStore, rs: torch.Tensor,
-                     cold: torch.Tensor | None = None) -> torch.Tensor:
+                     staged: bool = False) -> torch.Tensor:
     """Â[P_g, :] · X with X read from the store (whose rows carry the column
-    scale); the row scale is applied here.  ``cold``: the store's HBM staging
-    buffer holding this epoch's copy of the cold rows (None: read them from
-    pinned host memory, zero-copy)."""
+    scale); the row scale is applied here.  ``staged``: read the cold rows from
+    the store's HBM staging buffer (this epoch's copy), else from pinned host
+    memory, zero-copy."""
     import ctypes as C
     from . import _lib as L
     F = store.F
@@ -66,8 +67,9 @@ def _store_aggregate(tiles_g: T.Tiles, store: FeatureStore, rs: torch.Tensor,
     full = torch.empty(((W + 1) * 8, F), dtype=torch.float32, device=rs.device)
     sc = tiles_g.scratch()
     s = tiles_g.struct()
-    cold_ptr = store.cpu_ptr if cold is None else cold.data_ptr()
-    L.call("tcc_cnic_forward_mixed", C.byref(s), None, C.c_void_p(store.id_map.data_ptr()),
+    cold_ptr = store.cold_stage.data_ptr() if staged else store.cpu_ptr
+    id_map = store.stage_id_map if staged else store.id_map
+    L.call("tcc_cnic_forward_mixed", C.byref(s), None, C.c_void_p(id_map.data_ptr()),
            C.c_void_p(cold_ptr), C.c_void_p(store.cache_search_map.data_ptr()),
            C.c_void_p(store.gpu_ptrs.data_ptr()), store.capacity, C.c_void_p(full.data_ptr()), F, 0,
            C.c_void_p(sc.data_ptr()), sc.numel(), C.c_void_p(torch.cuda.current_stream().cuda_stream))
@@ -149,7 +151,8 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
     # stream (the copy for epoch e + 1 overlaps the rest of epoch e), or read
     # zero-copy from pinned host memory by every gather that touches them
     store = R["store"]
-    staged = bool(cfg.get("cold_staging", True)) and store.enable_cold_staging()
+    staged = bool(cfg.get("cold_staging", True)) and store.enable_cold_staging(
+        columns=R["tiles_g"].sparseIdx, force_gather=bool(cfg.get("cold_stage_gather", False)))
     if staged:
         side = torch.cuda.Stream(device=device)
         ready = torch.cuda.Event()
@@ -164,7 +167,7 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
         opt.zero_grad(set_to_none=True)
         if staged:
             torch.cuda.current_stream().wait_event(ready)
-            Z1 = _store_aggregate(R["tiles_g"], store, R["rs"], cold=store.cold_stage)
+            Z1 = _store_aggregate(R["tiles_g"], store, R["rs"], staged=True)
             used.record()
             side.wait_event(used)
             store.stage_cold(side)  # next epoch's copy

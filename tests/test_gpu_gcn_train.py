@@ -42,13 +42,16 @@ def _dense_loss(cfg, device):
     return float(torch.nn.functional.cross_entropy(logits[idx], y, reduction="sum") / labeled.sum())
 
 
-@pytest.mark.parametrize("transform_first,cold_staging", [(False, True), (True, True), (False, False)])
-def test_gcn_trainer_matches_dense_reference(gpu, transform_first, cold_staging):
-    """Cold rows through the HBM staging buffer (default) and zero-copy."""
+@pytest.mark.parametrize("transform_first,cold_staging,gather", [
+    (False, True, False), (True, True, False), (False, False, False), (True, True, True)])
+def test_gcn_trainer_matches_dense_reference(gpu, transform_first, cold_staging, gather):
+    """Cold rows through the HBM staging buffer (bulk copy, or the row-gather
+    kernel reading the pinned host rows) and zero-copy."""
     cfg = train_gcn.config(shrink=10)
     cfg["dropout"] = 0.0
     cfg["epochs"] = 6
     cfg["cold_staging"] = cold_staging
+    cfg["cold_stage_gather"] = gather
     dev = torch.device("cuda", 0)
     r = train_gcn.train(cfg, dev, 1, 0, transform_first=transform_first)
     assert r["cold_staging"] == cold_staging
