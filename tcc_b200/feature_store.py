@@ -16,6 +16,23 @@ import numpy as np
 import torch
 
 
+def cold_stage_plan(columns: torch.Tensor, cache_search_map: torch.Tensor, id_map: torch.Tensor,
+                    num_nodes: int):
+    """Which cold rows an aggregation over ``columns`` reads, and where they go
+    in a compact staging buffer.  Returns (cold, ids, stage_map): ``cold`` the
+    sorted cold column ids among ``columns`` (ids outside [0, num_nodes) are
+    padding), ``ids`` their rows in the host cold block (id_map[cold]), and
+    ``stage_map`` [num_nodes] int32 with stage_map[cold[i]] = i and -1
+    elsewhere -- the id map an aggregation reading the staging buffer uses."""
+    c = torch.unique(columns.to(dtype=torch.int64))
+    c = c[(c >= 0) & (c < num_nodes)]
+    c = c[cache_search_map.to(c.device)[c] < 0]
+    ids = id_map.to(c.device)[c].to(torch.int64)
+    stage_map = torch.full((num_nodes,), -1, dtype=torch.int32, device=c.device)
+    stage_map[c] = torch.arange(c.numel(), dtype=torch.int32, device=c.device)
+    return c, ids, stage_map
+
+
 class FeatureStore:
     """Features X [num_nodes x F] split by degree into an HBM part and a pinned
     host part.  ``hot_fraction`` of the nodes (highest degree first) go to HBM."""
@@ -68,13 +85,12 @@ class FeatureStore:
         if self.n_cold == 0:
             return False
         device = self.gpu_rows.device
-        ids = None
+        ids = stage_map = None
         if columns is not None:
-            c = torch.unique(columns.to(device=device, dtype=torch.int64))
-            c = c[(c >= 0) & (c < self.num_nodes)]
-            c = c[self.cache_search_map[c] < 0]
-            if c.numel() < self.n_cold or force_gather:
-                ids = self.id_map[c].to(torch.int64)
+            c, ids, stage_map = cold_stage_plan(columns.to(device), self.cache_search_map, self.id_map,
+                                                self.num_nodes)
+            if c.numel() == self.n_cold and not force_gather:
+                ids = stage_map = None
         n_stage = self.n_cold if ids is None else ids.numel()
         if budget_bytes is None:
             free, _ = torch.cuda.mem_get_info(device)
@@ -87,8 +103,6 @@ class FeatureStore:
             self.stage_id_map = self.id_map
         else:
             self.stage_ids = ids
-            stage_map = torch.full((self.num_nodes,), -1, dtype=torch.int32, device=device)
-            stage_map[c] = torch.arange(c.numel(), dtype=torch.int32, device=device)
             self.stage_id_map = stage_map
         return True
 
