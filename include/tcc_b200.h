@@ -83,6 +83,18 @@ typedef struct tcc_swtcf {
     void* pull_plan;
     uint64_t pull_plan_bytes;
     int32_t pull_plan_ready;
+    /* row-window (BCSR) tiling of the same matrix for the forward pull, built
+     * only by tcc_swtcf_prepare_pull and owned by the matrix; a conversion
+     * marks it stale (fwd_ready = 0) and tcc_swtcf_free releases it */
+    int32_t fwd_ready;
+    uint32_t* fwdRowWindowOffset;        /* [ceil(rows/8)+1] */
+    uint32_t* fwdTcOffset;               /* [fwd_tiles+1] */
+    uint32_t* fwdSparseA2B;              /* [8*fwd_tiles] */
+    uint64_t* fwdTcLocalBit;             /* [fwd_tiles] */
+    uint64_t fwd_tiles;
+    void* fwd_plan;
+    uint64_t fwd_plan_bytes;
+    int32_t fwd_plan_ready;
 } tcc_swtcf;
 
 typedef struct tcc_swtcf_workspace tcc_swtcf_workspace; /* opaque */
@@ -120,6 +132,17 @@ tcc_status tcc_swtcf_sizes(const tcc_swtcf* m, cudaStream_t stream, uint64_t* nu
  * superWindowSize == 16, like the reference. */
 tcc_status tcc_swtcf_spmm(const tcc_swtcf* m, const float* X, float* Y, uint32_t tc_threshold,
                           cudaStream_t stream);
+/* No reference counterpart.  Builds, once per conversion, a row-window tiling
+ * of the converted matrix owned by m (allocates device memory: about 40 B per
+ * tile plus a transient workspace of the conversion's size; synchronises the
+ * stream).  Until the next conversion, tcc_swtcf_spmm and tcc_swtcf_spmm_ex
+ * then run the forward product as a pull over those row windows (each output
+ * row written by its window, no reductions) instead of the push over column
+ * windows; the TF32 / fp32 choice by tc_threshold then applies to the
+ * row-window tiles, so results differ from the push's by TF32 rounding on
+ * different tiles (within the reference's 1e-3 bound).  Without this call the
+ * forward entry points allocate nothing, like the reference's. */
+tcc_status tcc_swtcf_prepare_pull(tcc_swtcf* m, cudaStream_t stream);
 /* launchSWTCFSpMMQuantized (include/swtcf_spmm.cuh:18-26; src/swtcf_spmm.cu:
  * 268-432, 469-502): Y[numDst x 128] += pattern(A) * Xq where source column c
  * reads global node g = src_global[c] (NULL: g = c) and uses the int8 row

@@ -40,7 +40,11 @@ class Swtcf(C.Structure):
                 ("tileRowSlot", C.c_void_p), ("tileLocalBit", C.c_void_p),
                 ("capacity_tiles", C.c_uint64), ("capacity_rows", C.c_uint64),
                 ("pull_plan", C.c_void_p), ("pull_plan_bytes", C.c_uint64),
-                ("pull_plan_ready", C.c_int32)]
+                ("pull_plan_ready", C.c_int32), ("fwd_ready", C.c_int32),
+                ("fwdRowWindowOffset", C.c_void_p), ("fwdTcOffset", C.c_void_p),
+                ("fwdSparseA2B", C.c_void_p), ("fwdTcLocalBit", C.c_void_p),
+                ("fwd_tiles", C.c_uint64), ("fwd_plan", C.c_void_p),
+                ("fwd_plan_bytes", C.c_uint64), ("fwd_plan_ready", C.c_int32)]
 
 
 class Bcsr(C.Structure):
@@ -77,6 +81,7 @@ PROTOTYPES = {
     "tcc_swtcf_workspace_device_error": (_st, [_vp, _vp, C.POINTER(_u32)]),
     "tcc_swtcf_sizes": (_st, [C.POINTER(Swtcf), _vp, C.POINTER(_u64), C.POINTER(_u64)]),
     "tcc_swtcf_spmm": (_st, [C.POINTER(Swtcf), _vp, _vp, _u32, _vp]),
+    "tcc_swtcf_prepare_pull": (_st, [C.POINTER(Swtcf), _vp]),
     "tcc_swtcf_spmm_quantized": (_st, [C.POINTER(Swtcf), _vp, _vp, _vp, _vp, _u32, _vp]),
     "tcc_swtcf_spmm_ex": (_st, [C.POINTER(Swtcf), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
                                 _i, _vp]),

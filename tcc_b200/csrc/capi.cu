@@ -186,9 +186,23 @@ tcc_status tcc_swtcf_alloc(tcc_swtcf* m, uint32_t rows, uint32_t cols, uint32_t 
     });
 }
 
+static void release_fwd(tcc_swtcf* m) {
+    cudaFree(m->fwdRowWindowOffset);
+    cudaFree(m->fwdTcOffset);
+    cudaFree(m->fwdSparseA2B);
+    cudaFree(m->fwdTcLocalBit);
+    cudaFree(m->fwd_plan);
+    m->fwdRowWindowOffset = m->fwdTcOffset = m->fwdSparseA2B = nullptr;
+    m->fwdTcLocalBit = nullptr;
+    m->fwd_plan = nullptr;
+    m->fwd_tiles = m->fwd_plan_bytes = 0;
+    m->fwd_ready = m->fwd_plan_ready = 0;
+}
+
 tcc_status tcc_swtcf_free(tcc_swtcf* m) {
     return guarded("tcc_swtcf_free", [&] {
         if (!m) return;
+        release_fwd(m);
         cudaFree(m->superWindowRowOffset);
         cudaFree(m->superWindowRows);
         cudaFree(m->superWindowRowCacheSlot);
@@ -224,6 +238,7 @@ tcc_status tcc_swtcf_convert_coo(const uint32_t* d_dst, const uint32_t* d_src, u
         TCC_REQUIRE(ws && out && d_dst && d_src, "null argument");
         tcc::swtcf_convert(d_dst, d_src, nullptr, nullptr, nnz, out, ws->impl, stream);
         out->pull_plan_ready = 0;
+        out->fwd_ready = 0;
     });
 }
 
@@ -235,6 +250,7 @@ tcc_status tcc_swtcf_convert_csr(const uint64_t* d_rowptr, const uint32_t* d_col
         TCC_REQUIRE(rows == out->rows, "CSR row count differs from the matrix's rows");
         tcc::swtcf_convert(nullptr, nullptr, d_rowptr, d_col, nnz, out, ws->impl, stream);
         out->pull_plan_ready = 0;
+        out->fwd_ready = 0;
     });
 }
 
@@ -279,13 +295,66 @@ static tcc::PushTiles swtcf_push(const tcc_swtcf* m) {
     return t;
 }
 
+// The prepared row-window tiling as a pull operand (tcc_swtcf_prepare_pull).
+static tcc::PullTiles swtcf_fwd_pull(const tcc_swtcf* m) {
+    tcc::PullTiles t{};
+    t.num_windows = (m->rows + 7) / 8;
+    t.num_tiles = (uint32_t)m->fwd_tiles;
+    t.win_offset = m->fwdRowWindowOffset;
+    t.bits = m->fwdTcLocalBit;
+    t.idx = m->fwdSparseA2B;
+    t.bits_transposed = false;
+    t.num_out = m->rows;
+    t.num_in = m->cols;
+    return t;
+}
+
+static void swtcf_forward(const tcc_swtcf* m, const tcc::Dense& d, uint32_t tc_threshold,
+                          int accumulate, cudaStream_t stream) {
+    if (m->fwd_ready) {
+        tcc::pull_spmm(swtcf_fwd_pull(m), d, tc_threshold, accumulate, m->fwd_plan,
+                       m->fwd_plan_bytes, m->fwd_plan_ready != 0, nullptr, stream);
+        const_cast<tcc_swtcf*>(m)->fwd_plan_ready = 1;
+        return;
+    }
+    if (!accumulate) zero_rows(d.Y, d.ldy, d.F, m->rows, stream);
+    tcc::push_spmm(swtcf_push(m), d, tc_threshold, nullptr, stream);
+}
+
+tcc_status tcc_swtcf_prepare_pull(tcc_swtcf* m, cudaStream_t stream) {
+    return guarded("tcc_swtcf_prepare_pull", [&] {
+        TCC_REQUIRE(m && m->colWindowOffset, "null or unallocated matrix");
+        release_fwd(m);
+        tcc::TilesWorkspace ws(std::max<uint64_t>(m->nnz, 1), m->rows, m->cols);
+        const uint64_t T = tcc::tiles_prepare_swtcf(ws, m, stream);
+        const uint32_t W = (m->rows + 7) / 8;
+        try {
+            dev_alloc(&m->fwdRowWindowOffset, (uint64_t)W + 1);
+            dev_alloc(&m->fwdTcOffset, T + 1);
+            dev_alloc(&m->fwdSparseA2B, 8 * T);
+            dev_alloc(&m->fwdTcLocalBit, T);
+            tcc::tiles_fill(ws, TCC_TILES_BCSR, m->fwdRowWindowOffset, m->fwdTcOffset,
+                            m->fwdSparseA2B, m->fwdTcLocalBit, stream);
+            m->fwd_plan_bytes = tcc::pull_scratch_bytes(W, T);
+            TCC_CUDA(cudaMalloc(&m->fwd_plan, m->fwd_plan_bytes));
+            m->fwd_tiles = T;
+            // the workspace is freed on return: finish the fill first
+            TCC_CUDA(cudaStreamSynchronize(stream));
+            m->fwd_ready = 1;
+        } catch (...) {
+            release_fwd(m);
+            throw;
+        }
+    });
+}
+
 tcc_status tcc_swtcf_spmm(const tcc_swtcf* m, const float* X, float* Y, uint32_t tc_threshold,
                           cudaStream_t stream) {
     return guarded("tcc_swtcf_spmm", [&] {
         TCC_REQUIRE(m && X && Y, "null argument");
         TCC_REQUIRE(m->superWindowSize == 16, "SWTCF SpMM requires superWindowSize=16");
         tcc::Dense d{X, 128, Y, 128, 128, nullptr, nullptr};
-        tcc::push_spmm(swtcf_push(m), d, tc_threshold, nullptr, stream);
+        swtcf_forward(m, d, tc_threshold, 1, stream);
     });
 }
 
@@ -310,9 +379,8 @@ tcc_status tcc_swtcf_spmm_ex(const tcc_swtcf* m, const float* X, uint64_t ldx, f
                              cudaStream_t stream) {
     return guarded("tcc_swtcf_spmm_ex", [&] {
         TCC_REQUIRE(m && X && Y, "null argument");
-        if (!accumulate) zero_rows(Y, ldy, F, m->rows, stream);
         tcc::Dense d{X, ldx, Y, ldy, F, row_scale, col_scale};
-        tcc::push_spmm(swtcf_push(m), d, tc_threshold, nullptr, stream);
+        swtcf_forward(m, d, tc_threshold, accumulate, stream);
     });
 }
 

@@ -71,6 +71,46 @@ __global__ void keys_from_csr_kernel(const uint64_t* __restrict__ rowptr,
     vals[i] = x & 7u;
 }
 
+// SWTCF tile t of column window w (the largest w with col_off[w] <= t): each
+// set bit (localRow r, localCol c) is the nonzero (sw_rows[sw_off[w/S] +
+// slots[8t + r]], 8w + c), written as a row-window key at pos[t], pos[t] + 1, ...
+// (pos = exclusive prefix of the tile popcounts).
+__global__ void keys_from_swtcf_kernel(const uint32_t* __restrict__ col_off, uint32_t W, uint32_t S,
+                                       const uint32_t* __restrict__ sw_off,
+                                       const uint32_t* __restrict__ sw_rows,
+                                       const uint32_t* __restrict__ slots,
+                                       const uint64_t* __restrict__ bits,
+                                       const uint32_t* __restrict__ pos, uint32_t T, uint32_t rows,
+                                       uint32_t cols, int ybits, uint64_t* __restrict__ keys,
+                                       uint32_t* __restrict__ vals, uint32_t* err) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    uint32_t lo = 0, hi = W - 1;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo + 1) / 2;
+        if (col_off[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    const uint32_t w = lo;
+    const uint32_t swoff = sw_off[w / S];
+    unsigned long long b = bits[t];
+    uint32_t p = pos[t];
+    while (b) {
+        const int k = __ffsll((long long)b) - 1;
+        b &= b - 1;
+        const uint32_t slot = slots[(uint64_t)t * 8 + (k >> 3)];
+        uint32_t row = slot == 0xFFFFFFFFu ? rows : sw_rows[swoff + slot];
+        uint32_t col = w * 8 + (k & 7);
+        if (row >= rows || col >= cols) {
+            raise_error(err, TCC_DEVERR_INDEX_RANGE);
+            row = 0;
+            col = 0;
+        }
+        keys[p] = ((uint64_t)(row >> 3) << ybits) | col;
+        vals[p] = row & 7u;
+        ++p;
+    }
+}
+
 // ---------------------------------------------------------------- step 3 --
 __global__ void mark_heads_kernel(const uint64_t* __restrict__ keys, uint64_t n,
                                   uint32_t* __restrict__ head) {
@@ -546,6 +586,8 @@ TilesWorkspace::TilesWorkspace(uint64_t nnz_capacity, uint32_t rows, uint32_t co
 
 TilesWorkspace::~TilesWorkspace() { cudaFree(arena.base); }
 
+static uint64_t finish_prepare(TilesWorkspace& ws, cudaStream_t s);
+
 uint64_t tiles_prepare(TilesWorkspace& ws, int kind, const uint64_t* d_rowptr,
                        const uint32_t* d_col, uint32_t rows, uint32_t cols, uint64_t nnz,
                        cudaStream_t s) {
@@ -567,6 +609,11 @@ uint64_t tiles_prepare(TilesWorkspace& ws, int kind, const uint64_t* d_rowptr,
             ws.g.vals, ws.small);
     build_windows(ws.g, nnz, wbits + ws.ybits, ws.ybits, ws.W, ws.wcnt, ws.wgstart, ws.tiles,
                   ws.off, ws.small, ws.tmp, s);
+    return finish_prepare(ws, s);
+}
+
+// Reads back the error word, group and tile counts after build_windows.
+static uint64_t finish_prepare(TilesWorkspace& ws, cudaStream_t s) {
     uint32_t host[2] = {0, 0};
     TCC_CUDA(cudaMemcpyAsync(host, ws.small, 8, cudaMemcpyDeviceToHost, s));
     uint32_t T = 0;
@@ -581,6 +628,40 @@ uint64_t tiles_prepare(TilesWorkspace& ws, int kind, const uint64_t* d_rowptr,
     ws.T = T;
     ws.prepared = true;
     return T;
+}
+
+uint64_t tiles_prepare_swtcf(TilesWorkspace& ws, const tcc_swtcf* m, cudaStream_t s) {
+    TCC_REQUIRE(m->rows > 0 && m->cols > 0, "empty matrix shape");
+    TCC_REQUIRE(m->rows <= ws.rows && m->cols <= ws.cols, "tiles workspace smaller than the matrix");
+    uint32_t Tsw = 0;
+    TCC_CUDA(cudaMemcpyAsync(&Tsw, m->colWindowOffset + m->numColWindows, 4, cudaMemcpyDeviceToHost, s));
+    TCC_CUDA(cudaStreamSynchronize(s));
+    TCC_REQUIRE(Tsw <= ws.E, "tiles workspace smaller than the matrix");
+    ws.kind = TCC_TILES_BCSR;
+    ws.cur_rows = m->rows;
+    ws.cur_cols = m->cols;
+    ws.W = (m->rows + 7) / 8;
+    ws.ybits = std::max(1, bits_for(m->cols));
+    const int wbits = std::max(1, bits_for(ws.W));
+    TCC_CUDA(cudaMemsetAsync(ws.small, 0, 64, s));
+    uint32_t nnz = 0;
+    if (Tsw) {
+        // tile popcounts -> write positions (the group buffers' head/excl are
+        // free until build_windows); total at small[8]
+        popcount_kernel<<<blocks(Tsw), kThreads, 0, s>>>(m->tileLocalBit, Tsw, ws.g.head);
+        exclusive_scan<uint32_t>(ws.g.head, ws.g.excl, Tsw, ws.small + 8, ws.tmp, s);
+        TCC_CUDA(cudaMemcpyAsync(&nnz, ws.small + 8, 4, cudaMemcpyDeviceToHost, s));
+        TCC_CUDA(cudaStreamSynchronize(s));
+        TCC_REQUIRE(nnz <= ws.E, "tiles workspace smaller than the matrix");
+        keys_from_swtcf_kernel<<<blocks(Tsw), kThreads, 0, s>>>(
+            m->colWindowOffset, m->numColWindows, m->superWindowSize, m->superWindowRowOffset,
+            m->superWindowRows, m->tileRowSlot, m->tileLocalBit, ws.g.excl, Tsw, m->rows, m->cols,
+            ws.ybits, ws.g.keys, ws.g.vals, ws.small);
+    }
+    ws.nnz = nnz;
+    build_windows(ws.g, nnz, wbits + ws.ybits, ws.ybits, ws.W, ws.wcnt, ws.wgstart, ws.tiles,
+                  ws.off, ws.small, ws.tmp, s);
+    return finish_prepare(ws, s);
 }
 
 void tiles_fill(TilesWorkspace& ws, int kind, uint32_t* win_offset, uint32_t* tc_offset,

@@ -61,6 +61,9 @@ void swtcf_convert(const uint32_t* d_dst, const uint32_t* d_src, const uint64_t*
 uint64_t tiles_prepare(TilesWorkspace& ws, int kind, const uint64_t* d_rowptr,
                        const uint32_t* d_col, uint32_t rows, uint32_t cols, uint64_t nnz,
                        cudaStream_t s);
+// SWTCF tiles -> the same matrix as row-window (BCSR) tiles: prepare
+// (synchronises, returns T), then tiles_fill with TCC_TILES_BCSR.
+uint64_t tiles_prepare_swtcf(TilesWorkspace& ws, const tcc_swtcf* m, cudaStream_t s);
 void tiles_fill(TilesWorkspace& ws, int kind, uint32_t* win_offset, uint32_t* tc_offset,
                 uint32_t* idx, uint64_t* bits, cudaStream_t s);
 

@@ -319,10 +319,10 @@ __global__ void __launch_bounds__(kTW * 32, 1)
                                        acc[4 * p + 3][e]);
                 v = f4_scale(v, rsc);
                 float* yp = yrow + f;
-                if (red) {
+                // accumulate: a reduction, not load + add + store (the same fp32
+                // add, without a DRAM round trip stalling the warp's copy ring)
+                if (red || accumulate) {
                     red_add_v4(yp, v);
-                } else if (accumulate) {
-                    *reinterpret_cast<float4*>(yp) = f4_add(*reinterpret_cast<const float4*>(yp), v);
                 } else {
                     __stcs(reinterpret_cast<float4*>(yp), v);
                 }

@@ -283,11 +283,10 @@ __global__ void __launch_bounds__(kPullWarps * 32, 2) pull_kernel(PullTiles a, D
                                        dacc[4 * p + 3][e]);
                 v = f4_scale(v, rsc);
                 float* yp = yrow + f;
-                if (heavy) {
+                // accumulate: a reduction, not load + add + store (the same fp32
+                // add, without a DRAM round trip in the epilogue)
+                if (heavy || accumulate) {
                     red_add_v4(yp, v);
-                } else if (accumulate) {
-                    const float4 o = *reinterpret_cast<float4*>(yp);
-                    *reinterpret_cast<float4*>(yp) = f4_add(o, v);
                 } else {
                     __stcs(reinterpret_cast<float4*>(yp), v);
                 }

@@ -174,6 +174,14 @@ def convert_csr(rowptr: torch.Tensor, col: torch.Tensor, m: SWTCFMatrix,
            C.byref(m.c), ws.h, _stream(stream))
 
 
+def prepare_pull(m: SWTCFMatrix, stream=None):
+    """Build the converted matrix's row-window tiling (no reference
+    counterpart; allocates, synchronises).  Until the next conversion,
+    ``spmm`` and ``spmm_ex`` run the forward product as a pull over row windows
+    instead of the push over column windows."""
+    L.call("tcc_swtcf_prepare_pull", C.byref(m.c), _stream(stream))
+
+
 def spmm(m: SWTCFMatrix, X: torch.Tensor, Y: torch.Tensor,
          tc_threshold: int = DEFAULT_TC_THRESHOLD, stream=None):
     """launchSWTCFSpMM (src/swtcf_spmm.cu:437-466): Y[rows x 128] += A X[cols x 128]."""

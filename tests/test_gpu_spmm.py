@@ -276,3 +276,39 @@ def test_push_heavy_hub_window(gpu, oracle, thr):
         Yz = torch.zeros((g.rows, 128), device="cuda")
         swtcf.spmm(m, dense(X), Yz, tc_threshold=12)
         assert rel_inf(Yz.cpu().numpy(), ref) <= REF_TOL
+
+
+@pytest.mark.parametrize("name,g", CASES, ids=[c[0] for c in CASES])
+def test_swtcf_spmm_prepared_pull(gpu, oracle, name, g):
+    """tcc_swtcf_prepare_pull: the forward product as a pull over a row-window
+    tiling of the converted matrix.  Against the oracle (fp32 tiles at
+    tc_threshold 65, TF32 at 12; Y accumulates like the reference), the
+    reference kernel, and the general form with scales; a new conversion
+    drops the tiling and the push runs again."""
+    m = make_swtcf(g)
+    X = G.features(g.cols, 128, seed=41)
+    Y0 = G.features(g.rows, 128, seed=42)
+    swtcf.prepare_pull(m)
+    assert m.c.fwd_ready == 1
+    want = oracle.csr_spmm(g, X) + Y0
+    for thr, tol in ((65, FP32_TOL), (12, TF32_TOL)):
+        Yd = dense(Y0)
+        swtcf.spmm(m, dense(X), Yd, tc_threshold=thr)
+        assert rel_fro(Yd.cpu().numpy(), want) <= tol, (name, thr)
+    if oracle.ref_lib() is None:
+        pytest.fail("oracle/_ref/libtcc_ref.so missing: run `make -C oracle ref` before shipping")
+    dst, src = g.coo()
+    ref, _ = oracle.ref_swtcf_spmm(g.rows, g.cols, dst, src, X, tc_threshold=12)
+    Yz = torch.zeros((g.rows, 128), device="cuda")
+    swtcf.spmm(m, dense(X), Yz, tc_threshold=12)
+    assert rel_inf(Yz.cpu().numpy(), ref) <= REF_TOL, name
+    rs, cs = G.gcn_scales(g) if g.rows == g.cols else G.row_scales(g)
+    Ys = swtcf.spmm_ex(m, dense(X), tc_threshold=65, row_scale=dense(rs),
+                       col_scale=None if cs is None else dense(cs))
+    assert rel_fro(Ys.cpu().numpy(), oracle.csr_spmm(g, X, rs, cs)) <= FP32_TOL, name
+    ws = swtcf.SWTCFConvertWorkspace(g.nnz, g.cols, 16)
+    swtcf.convert_coo(u32(dst), u32(src), m, ws)
+    assert m.c.fwd_ready == 0
+    Yd = dense(Y0)
+    swtcf.spmm(m, dense(X), Yd, tc_threshold=65)
+    assert rel_fro(Yd.cpu().numpy(), want) <= FP32_TOL, name
