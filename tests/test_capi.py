@@ -45,6 +45,11 @@ def test_null_arguments_are_rejected_without_a_gpu(lib):
     assert lib.tcc_swtcf_alloc(C.byref(m), 4, 0, 4, 16) == 1          # cols == 0
     assert lib.tcc_swtcf_alloc(C.byref(m), 4, 4, 4, 33) == 1          # S > 32
     assert lib.tcc_swtcf_spmm(None, None, None, 12, None) == 1
+    assert lib.tcc_swtcf_prepare_pull(None, None) == 1
+    assert lib.tcc_swtcf_prepare_pull(C.byref(_lib.Swtcf()), None) == 1  # never allocated
+    assert b"unallocated" in lib.tcc_last_error()
+    # the ctypes mirror of tcc_swtcf ends with the forward-pull fields
+    assert _lib.Swtcf._fields_[-1][0] == "fwd_plan_ready"
     assert lib.tcc_bcsr_spmm(None, None, 0, None, 0, 128, 12, None, None, 0, None, 0, 0, None) == 1
     ws = C.c_void_p()
     assert lib.tcc_swtcf_workspace_create(C.byref(ws), 0, 10, 16) == 1
