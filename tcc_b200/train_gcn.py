@@ -155,6 +155,7 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
         columns=R["tiles_g"].sparseIdx, force_gather=bool(cfg.get("cold_stage_gather", False)))
     if staged:
         side = torch.cuda.Stream(device=device)
+        store.cold_stage.record_stream(side)  # written on the side stream
         ready = torch.cuda.Event()
         used = torch.cuda.Event()
         store.stage_cold(side)
@@ -163,15 +164,17 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
     drop.manual_seed(cfg["seed"] * 1000 + rank)
     cls_pad = (cfg["classes"] + 3) // 4 * 4  # transform-first SpMM width, multiple of 4
 
-    def epoch():
+    def epoch(stage_next: bool):
         opt.zero_grad(set_to_none=True)
         if staged:
+            # an unfinished copy shows up here, in this epoch's time
             torch.cuda.current_stream().wait_event(ready)
             Z1 = _store_aggregate(R["tiles_g"], store, R["rs"], staged=True)
-            used.record()
-            side.wait_event(used)
-            store.stage_cold(side)  # next epoch's copy
-            ready.record(side)
+            if stage_next:  # next epoch's copy, overlapping the rest of this one
+                used.record()
+                side.wait_event(used)
+                store.stage_cold(side)
+                ready.record(side)
         else:
             Z1 = _store_aggregate(R["tiles_g"], store, R["rs"])
         H1 = torch.relu(Z1 @ W1)
@@ -199,18 +202,22 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
         return lt
 
     times, losses = [], []
-    for _ in range(start_epoch, cfg["epochs"]):
-        torch.cuda.synchronize()
+    for e in range(start_epoch, cfg["epochs"]):
+        # only this stream: a side-stream copy still running is waited for
+        # inside the next epoch (and timed there), not between epochs
+        torch.cuda.current_stream().synchronize()
         if world > 1:
             dist.barrier()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        lt = epoch()
+        lt = epoch(stage_next=e + 1 < cfg["epochs"])
         b.record()
-        torch.cuda.synchronize()
+        b.synchronize()
         times.append(a.elapsed_time(b) / 1e3)
         losses.append(float(lt))
+    if staged:
+        side.synchronize()
     if cfg.get("save") and rank == 0:  # weights are identical on every rank
         torch.save({"W1": W1.detach(), "W2": W2.detach(), "opt": opt.state_dict(),
                     "epoch": cfg["epochs"], "config": {k: v for k, v in cfg.items()
