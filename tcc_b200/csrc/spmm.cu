@@ -137,7 +137,8 @@ __device__ __forceinline__ const float* store_row(const FeatureStore& fs, uint32
 
 // ---------------------------------------------------------------- pull ----
 // One warp per chunk; the 8 gather rows of a tile go straight to registers
-// as 128-bit L1::no_allocate loads in MMA fragment order, two tiles in flight
+// as 128-bit read-only loads in MMA fragment order (L1::no_allocate measured
+// slower in gather probes), two tiles in flight
 // per warp, 16 warps/SM.  Chunk metadata (bitmaps, gather indices) is
 // double-buffered in shared memory with cp.async one chunk ahead.
 constexpr int kPullWarps = 8;
