@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload spmm|gcn4|config5] [--dist-mode replicated|exchange]
 
-Workload: seeded R-MAT graph, 2^20 nodes, 16M directed
+Workload (config 2 of the benchmark set): seeded R-MAT graph, 2^20 nodes, 16M directed
 edges (a,b,c,d = 0.57,0.19,0.19,0.05) symmetrised, deduplicated, self-loops
 added; GCN normalisation D^-1/2 (A+I) D^-1/2 fused as diagonal scales; X, G
 fp32 [N x 128] ~ N(0,1).  One step = forward SpMM A.X plus the transposed SpMM
@@ -35,8 +35,10 @@ import json
 import os
 import re
 import statistics
+import shutil
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -126,11 +128,11 @@ class ClockSampler:
 
     def __init__(self, device_index):
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+        self.dir = tempfile.mkdtemp(prefix="tcc_clocks_")
+        self.path = os.path.join(self.dir, f"clocks_rank{device_index}.csv")
         self.idx = device_index
 
     def start(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
@@ -168,6 +170,7 @@ class ClockSampler:
                 for nm, v in zip(names, parts[5:9]):
                     if v.lower().startswith("active"):
                         reasons.add(nm)
+        shutil.rmtree(self.dir, ignore_errors=True)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),

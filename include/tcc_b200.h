@@ -50,7 +50,8 @@ typedef int tcc_status;
 #define TCC_DEVERR_HASH_LOOKUP 3
 #define TCC_DEVERR_OCCURRENCE 4    /* row occurrence above the super-window size */
 #define TCC_DEVERR_INDEX_RANGE 5   /* an input index >= rows/cols */
-#define TCC_DEVERR_WAIT_TIMEOUT 6  /* an in-kernel wait for a TMA copy expired (2 s); the
+#define TCC_DEVERR_WAIT_TIMEOUT 6  /* an in-kernel wait for a TMA copy expired (the
+                                      limit of tcc_set_wait_limit_ns, 2 s by default); the
                                       kernel returned early and its output is incomplete */
 
 const char* tcc_last_error(void);
@@ -226,6 +227,17 @@ tcc_status tcc_pull_device_error(void* scratch, int* code, cudaStream_t stream);
 void tcc_set_grid_reserve(uint32_t sms);
 uint32_t tcc_get_grid_reserve(void);
 
+/* No counterpart in the reference (its kernels have no bounded waits).  Every
+ * mbarrier wait of the bulk-copy pull kernel gives up after this many
+ * nanoseconds, records TCC_DEVERR_WAIT_TIMEOUT in the pull scratch's error
+ * word (tcc_pull_device_error), waits for its own copies still in flight and
+ * returns, leaving the context usable.  Process-wide; applies to launches made
+ * after the call; 0 restores the default.  Limits below 200 us poll the
+ * barrier without suspending. */
+#define TCC_DEFAULT_WAIT_LIMIT_NS 2000000000ull
+void tcc_set_wait_limit_ns(uint64_t ns);
+uint64_t tcc_get_wait_limit_ns(void);
+
 /* No counterpart in the reference, whose multi-GPU path reads peer feature
  * caches inside the SpMM kernel (cnic/src/core/spmm_kernel.cu:145-147).  Packs
  * the rows a rank sends in the halo exchange of the row-partitioned SpMM:
@@ -263,6 +275,14 @@ tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float*
 tcc_status tcc_bcsr_spmm_noalloc(const tcc_bcsr* a, const float* B, uint64_t ldb, float* C,
                                  uint64_t ldc, uint32_t F, uint32_t tc_threshold, const float* rs,
                                  const float* cs, int accumulate, cudaStream_t stream);
+/* No counterpart in the reference.  The device error word of the built-in
+ * scratch that tcc_bcsr_spmm_noalloc uses on the current device (the caller
+ * has no pointer to pass to tcc_pull_device_error): TCC_DEVERR_WAIT_TIMEOUT
+ * when a pull kernel gave up waiting on one of its copies, so that result is
+ * incomplete.  Synchronises `stream`, stores the word in *code and clears it.
+ * The next tcc_bcsr_spmm_noalloc call also clears it: read it after each call
+ * whose result matters.  Allocates nothing. */
+tcc_status tcc_noalloc_device_error(int* code, cudaStream_t stream);
 /* tf32_spmm_bcsc + tf32_computeX128TransposePipe2_BCSC
  * (cnic/src/core/spmm_dispatcher.cu:235-302, spmm_kernel.cu:1844-2167): the
  * column-window push pass, C += diag(rs) * A * diag(cs) * B, accumulated with

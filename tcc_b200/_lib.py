@@ -20,6 +20,8 @@ TILES_BCSR = 0
 TILES_BCSC = 1
 DEVERR_GROUP_DEGREE = 1
 DEVERR_INDEX_RANGE = 5
+DEVERR_WAIT_TIMEOUT = 6
+DEFAULT_WAIT_LIMIT_NS = 2_000_000_000  # TCC_DEFAULT_WAIT_LIMIT_NS
 
 
 class TccError(RuntimeError):
@@ -96,11 +98,14 @@ PROTOTYPES = {
     "tcc_pull_device_error": (_st, [_vp, C.POINTER(_i), _vp]),
     "tcc_set_grid_reserve": (None, [_u32]),
     "tcc_get_grid_reserve": (_u32, []),
+    "tcc_set_wait_limit_ns": (None, [_u64]),
+    "tcc_get_wait_limit_ns": (_u64, []),
     "tcc_gather_rows": (_st, [_vp, _u64, _u64, _vp, _u64, _vp, _u64, _u32, _vp, _vp]),
     "tcc_bcsr_spmm": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i, _vp,
                             C.c_size_t, _i, _vp]),
     "tcc_bcsr_spmm_noalloc": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
                                     _i, _vp]),
+    "tcc_noalloc_device_error": (_st, [C.POINTER(_i), _vp]),
     "tcc_bcsr_spmm_t": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),
     "tcc_bcsc_spmm": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),
     "tcc_bcsc_spmm_t": (_st, [C.POINTER(Bcsc), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _i,

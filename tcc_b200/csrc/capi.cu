@@ -138,6 +138,24 @@ void check_bcsr(const tcc_bcsr* a) {
     TCC_REQUIRE(a && a->rowWindowOffset && a->tcLocalBit && a->sparseA2B, "BCSR arrays missing");
     TCC_REQUIRE(a->num_rowWindows == (a->num_rows + 7) / 8, "num_rowWindows != ceil(num_rows/8)");
 }
+// The SWTCF tiles as the operand of the transposed pull (column windows own
+// their outputs; gather rows through the super-window row slots).
+tcc::PullTiles swtcf_t_pull(const tcc_swtcf* m) {
+    tcc::PullTiles t{};
+    t.num_windows = m->numColWindows;
+    t.num_tiles = (uint32_t)m->capacity_tiles;
+    t.win_offset = m->colWindowOffset;
+    t.bits = m->tileLocalBit;
+    t.idx = m->tileRowSlot;
+    t.bits_transposed = true;
+    t.sw_offset = m->superWindowRowOffset;
+    t.sw_rows = m->superWindowRows;
+    t.S = m->superWindowSize;
+    t.num_out = m->cols;
+    t.num_in = m->rows;
+    return t;
+}
+
 void check_bcsc(const tcc_bcsc* a) {
     TCC_REQUIRE(a && a->colWindowOffset && a->tcLocalBit && a->sparseA2C, "BCSC arrays missing");
     TCC_REQUIRE(a->num_colWindows == (a->num_cols + 7) / 8, "num_colWindows != ceil(num_cols/8)");
@@ -239,6 +257,10 @@ tcc_status tcc_swtcf_convert_coo(const uint32_t* d_dst, const uint32_t* d_src, u
         tcc::swtcf_convert(d_dst, d_src, nullptr, nullptr, nnz, out, ws->impl, stream);
         out->pull_plan_ready = 0;
         out->fwd_ready = 0;
+        // the transposed pass's work plan, on the conversion's stream: ready
+        // whenever the tiles are
+        tcc::pull_plan(swtcf_t_pull(out), out->pull_plan, out->pull_plan_bytes, stream);
+        out->pull_plan_ready = 1;
     });
 }
 
@@ -251,6 +273,10 @@ tcc_status tcc_swtcf_convert_csr(const uint64_t* d_rowptr, const uint32_t* d_col
         tcc::swtcf_convert(nullptr, nullptr, d_rowptr, d_col, nnz, out, ws->impl, stream);
         out->pull_plan_ready = 0;
         out->fwd_ready = 0;
+        // the transposed pass's work plan, on the conversion's stream: ready
+        // whenever the tiles are
+        tcc::pull_plan(swtcf_t_pull(out), out->pull_plan, out->pull_plan_bytes, stream);
+        out->pull_plan_ready = 1;
     });
 }
 
@@ -312,9 +338,9 @@ static tcc::PullTiles swtcf_fwd_pull(const tcc_swtcf* m) {
 static void swtcf_forward(const tcc_swtcf* m, const tcc::Dense& d, uint32_t tc_threshold,
                           int accumulate, cudaStream_t stream) {
     if (m->fwd_ready) {
+        // plan built and synchronised by tcc_swtcf_prepare_pull
         tcc::pull_spmm(swtcf_fwd_pull(m), d, tc_threshold, accumulate, m->fwd_plan,
                        m->fwd_plan_bytes, m->fwd_plan_ready != 0, nullptr, stream);
-        const_cast<tcc_swtcf*>(m)->fwd_plan_ready = 1;
         return;
     }
     if (!accumulate) zero_rows(d.Y, d.ldy, d.F, m->rows, stream);
@@ -338,9 +364,12 @@ tcc_status tcc_swtcf_prepare_pull(tcc_swtcf* m, cudaStream_t stream) {
             m->fwd_plan_bytes = tcc::pull_scratch_bytes(W, T);
             TCC_CUDA(cudaMalloc(&m->fwd_plan, m->fwd_plan_bytes));
             m->fwd_tiles = T;
-            // the workspace is freed on return: finish the fill first
+            tcc::pull_plan(swtcf_fwd_pull(m), m->fwd_plan, m->fwd_plan_bytes, stream);
+            // the workspace is freed on return, and forwards on any stream
+            // reuse the plan: finish the fill and the plan first
             TCC_CUDA(cudaStreamSynchronize(stream));
             m->fwd_ready = 1;
+            m->fwd_plan_ready = 1;
         } catch (...) {
             release_fwd(m);
             throw;
@@ -390,23 +419,11 @@ tcc_status tcc_swtcf_spmm_t(const tcc_swtcf* m, const float* G, uint64_t ldg, fl
                             cudaStream_t stream) {
     return guarded("tcc_swtcf_spmm_t", [&] {
         TCC_REQUIRE(m && G && Z, "null argument");
-        tcc::PullTiles t{};
-        t.num_windows = m->numColWindows;
-        t.num_tiles = (uint32_t)m->capacity_tiles;
-        t.win_offset = m->colWindowOffset;
-        t.bits = m->tileLocalBit;
-        t.idx = m->tileRowSlot;
-        t.bits_transposed = true;
-        t.sw_offset = m->superWindowRowOffset;
-        t.sw_rows = m->superWindowRows;
-        t.S = m->superWindowSize;
-        t.num_out = m->cols;
-        t.num_in = m->rows;
         // Z = diag(cs) A^T diag(rs) G: G rows are scaled by rs, Z rows by cs
         tcc::Dense d{G, ldg, Z, ldz, F, col_scale, row_scale};
-        tcc::pull_spmm(t, d, tc_threshold, accumulate, m->pull_plan, m->pull_plan_bytes,
-                       m->pull_plan_ready != 0, nullptr, stream);
-        const_cast<tcc_swtcf*>(m)->pull_plan_ready = 1;
+        // the plan was built on the conversion's stream, right after the tiles
+        tcc::pull_spmm(swtcf_t_pull(m), d, tc_threshold, accumulate, m->pull_plan,
+                       m->pull_plan_bytes, m->pull_plan_ready != 0, nullptr, stream);
     });
 }
 
@@ -474,6 +491,10 @@ size_t tcc_pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
 
 void tcc_set_grid_reserve(uint32_t sms) { tcc::set_grid_reserve(sms); }
 uint32_t tcc_get_grid_reserve(void) { return tcc::grid_reserve(); }
+void tcc_set_wait_limit_ns(uint64_t ns) {
+    tcc::set_wait_limit_ns(ns ? ns : (uint64_t)TCC_DEFAULT_WAIT_LIMIT_NS);
+}
+uint64_t tcc_get_wait_limit_ns(void) { return tcc::wait_limit_ns(); }
 
 tcc_status tcc_gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, const int64_t* idx,
                            uint64_t n, float* out, uint64_t ldo, uint32_t F, uint32_t* bad_flag,
@@ -522,11 +543,25 @@ tcc_status tcc_bcsr_spmm_noalloc(const tcc_bcsr* a, const float* B, uint64_t ldb
                                  " bytes of plan scratch; the built-in scratch holds " +
                                  std::to_string((size_t)TCC_NOALLOC_SCRATCH_BYTES) +
                                  " (use tcc_bcsr_spmm with caller scratch)");
-        // the shared array keeps the last call's plan: always rebuild it (the
-        // rebuild clears the plan header that must start at zero)
+        // the shared array keeps the last call's contents: the plan is rebuilt
+        // (or, for the kernels that need none, only the header cleared) every
+        // call, which also zeroes the error word; no later call reuses it
         tcc::Dense d{B, ldb, C, ldc, F, rs, cs};
         tcc::pull_spmm(bcsr_pull(a), d, tc_threshold, accumulate, noalloc_scratch(),
-                       TCC_NOALLOC_SCRATCH_BYTES, false, nullptr, stream);
+                       TCC_NOALLOC_SCRATCH_BYTES, false, nullptr, stream, /*keep_plan=*/false);
+    });
+}
+
+tcc_status tcc_noalloc_device_error(int* code, cudaStream_t stream) {
+    return guarded("tcc_noalloc_device_error", [&] {
+        TCC_REQUIRE(code, "code must not be NULL");
+        uint32_t* word = reinterpret_cast<uint32_t*>(static_cast<char*>(noalloc_scratch()) +
+                                                     tcc::kPullErrorOffset);
+        uint32_t v = 0;
+        TCC_CUDA(cudaMemcpyAsync(&v, word, sizeof(v), cudaMemcpyDeviceToHost, stream));
+        TCC_CUDA(cudaMemsetAsync(word, 0, sizeof(v), stream));
+        TCC_CUDA(cudaStreamSynchronize(stream));
+        *code = (int)v;
     });
 }
 

@@ -49,6 +49,10 @@ int sm_count();
 int grid_sms();
 void set_grid_reserve(uint32_t sms);
 uint32_t grid_reserve();
+// Limit of the bounded mbarrier waits in the bulk-copy pull kernel
+// (tcc_set_wait_limit_ns; process-wide, 2 s by default).
+void set_wait_limit_ns(uint64_t ns);
+uint64_t wait_limit_ns();
 
 // ------------------------------------------------------------ device side --
 

@@ -30,9 +30,10 @@
 //   batches ahead in registers, one lane per gathered row, so neither the
 //   index stream nor the dependent scale loads stall the warp.
 //
-// Every mbarrier wait is bounded by %globaltimer; on expiry the kernel records
-// TCC_DEVERR_WAIT_TIMEOUT, waits (bounded) for its own copies in flight
-// and returns.
+// Every mbarrier wait is bounded by %globaltimer (the limit set by
+// tcc_set_wait_limit_ns, 2 s by default); on expiry the kernel records
+// TCC_DEVERR_WAIT_TIMEOUT, waits for its own copies in flight (bounded by
+// kDrainNs, whatever the limit) and returns.
 #include "spmm.cuh"
 #include "tile_mma.cuh"
 
@@ -53,7 +54,7 @@ constexpr uint32_t kStageBytes = 8 * (kMaxBox * 4 + kRowPad);
 constexpr uint32_t kBatch = 4;                   // tiles per metadata batch (8 lanes each)
 constexpr uint32_t kFlushTiles = 64;             // max tiles summed in one fp32 register chain
 constexpr uint32_t kPieces = 8;                  // tile-range pieces per warp
-constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr unsigned long long kDrainNs = 2000000000ull;  // bound of the drain after a failure
 
 struct __align__(16) StageMeta {
     float cs[8];              // column scale of gathered row k (0 for padding) at
@@ -96,13 +97,29 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for phase `parity` of the mbarrier; false after kWaitNs.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    if (mbar_try(bar, parity)) return true;
+// Non-blocking test of phase `parity`.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of the mbarrier; false once limit_ns have passed.
+// Limits shorter than one suspended try poll without suspending, so that the
+// limit, not the suspend hint, decides when the wait gives up.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+    const bool poll = limit_ns < kSuspendNs;
+    if (poll ? mbar_test(bar, parity) : mbar_try(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     for (;;) {
-        if (mbar_try(bar, parity)) return true;
-        if (globaltimer() - t0 > kWaitNs) return false;
+        if (globaltimer() - t0 >= limit_ns) return false;
+        if (poll ? mbar_test(bar, parity) : mbar_try(bar, parity)) return true;
     }
 }
 
@@ -205,7 +222,7 @@ __global__ void zero_reduced_kernel(const uint32_t* __restrict__ off, uint32_t W
 template <int NP, bool FULL>
 __global__ void __launch_bounds__(kTW * 32, 1)
     pull_tma_kernel(PullTiles a, Dense d, uint32_t bw, uint32_t thr, int accumulate,
-                    uint32_t* __restrict__ err) {
+                    uint32_t* __restrict__ err, unsigned long long wait_ns) {
     extern __shared__ unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -384,9 +401,9 @@ __global__ void __launch_bounds__(kTW * 32, 1)
                     cq = 0;
                     cpar ^= 1u;
                 }
-                bool ok = mbar_try(smem_u32(&sbar[q]), par);
+                bool ok = wait_ns >= kSuspendNs && mbar_try(smem_u32(&sbar[q]), par);
                 if (!__all_sync(0xffffffffu, ok))
-                    ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sbar[q]), par));
+                    ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sbar[q]), par, wait_ns));
                 if (!ok) {
                     failed = true;
                     fq = q;
@@ -434,7 +451,7 @@ __global__ void __launch_bounds__(kTW * 32, 1)
         // not consumed, in ring order from slot fq
         uint32_t q = fq, par = fpar;
         for (uint32_t u = t; u < T1 && u < t + kR; ++u) {
-            (void)mbar_wait(smem_u32(&sbar[q]), par);
+            (void)mbar_wait(smem_u32(&sbar[q]), par, kDrainNs);
             if (++q == (uint32_t)kR) {
                 q = 0;
                 par ^= 1u;
@@ -473,7 +490,8 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
              : bw < 64  ? pull_tma_kernel<1, false>
                         : pull_tma_kernel<2, false>;
     TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(a, d, bw, thr, accumulate, err);
+    k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(a, d, bw, thr, accumulate, err,
+                                                       (unsigned long long)wait_limit_ns());
     TCC_CUDA(cudaGetLastError());
 }
 

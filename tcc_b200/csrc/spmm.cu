@@ -41,10 +41,13 @@ int sm_count() {
 
 namespace {
 std::atomic<uint32_t> g_grid_reserve{0};
+std::atomic<uint64_t> g_wait_limit_ns{TCC_DEFAULT_WAIT_LIMIT_NS};
 }  // namespace
 
 void set_grid_reserve(uint32_t sms) { g_grid_reserve.store(sms); }
 uint32_t grid_reserve() { return g_grid_reserve.load(); }
+void set_wait_limit_ns(uint64_t ns) { g_wait_limit_ns.store(ns); }
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(); }
 
 int grid_sms() {
     const int n = sm_count();
@@ -617,9 +620,28 @@ size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
     return PlanLayout(num_windows, num_tiles).total;
 }
 
+// Work plan of the register-gather kernel in the scratch: chunk descriptors,
+// split windows and a zeroed header (which also clears the error word).
+void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStream_t s) {
+    if (a.num_windows == 0) return;
+    const PlanLayout L(a.num_windows, a.num_tiles);
+    TCC_REQUIRE(scratch && scratch_bytes >= L.total, "pull scratch smaller than tcc_pull_scratch_bytes()");
+    char* base = reinterpret_cast<char*>(scratch);
+    PlanHeader* hdr = reinterpret_cast<PlanHeader*>(base);
+    uint32_t* cstart = reinterpret_cast<uint32_t*>(base + L.cstart);
+    uint4* desc = reinterpret_cast<uint4*>(base + L.desc);
+    uint32_t* heavy = reinterpret_cast<uint32_t*>(base + L.heavy);
+    const uint32_t W = a.num_windows;
+    TCC_CUDA(cudaMemsetAsync(hdr, 0, sizeof(PlanHeader), s));
+    plan_count_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart);
+    exclusive_scan<uint32_t>(cstart, cstart, W, cstart + W, base + L.tmp, s);
+    plan_fill_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart, desc, heavy, hdr);
+    TCC_CUDA(cudaGetLastError());
+}
+
 void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int accumulate,
                void* scratch, size_t scratch_bytes, bool plan_ready, const FeatureStore* fs,
-               cudaStream_t s) {
+               cudaStream_t s, bool keep_plan) {
     TCC_REQUIRE(d.F > 0 && d.F % 4 == 0, "F must be a positive multiple of 4");
     TCC_REQUIRE(d.ldx % 4 == 0 && d.ldy % 4 == 0 && d.ldx >= d.F && d.ldy >= d.F,
                 "row strides must be multiples of 4 elements and >= F");
@@ -632,22 +654,24 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
     TCC_REQUIRE(scratch && scratch_bytes >= L.total, "pull scratch smaller than tcc_pull_scratch_bytes()");
     char* base = reinterpret_cast<char*>(scratch);
     PlanHeader* hdr = reinterpret_cast<PlanHeader*>(base);
-    uint32_t* cstart = reinterpret_cast<uint32_t*>(base + L.cstart);
     uint4* desc = reinterpret_cast<uint4*>(base + L.desc);
     uint32_t* heavy = reinterpret_cast<uint32_t*>(base + L.heavy);
-    const uint32_t W = a.num_windows;
-    if (!plan_ready) {
-        TCC_CUDA(cudaMemsetAsync(hdr, 0, sizeof(PlanHeader), s));
-        plan_count_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart);
-        exclusive_scan<uint32_t>(cstart, cstart, W, cstart + W, base + L.tmp, s);
-        plan_fill_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart, desc, heavy, hdr);
-    }
     static_assert(offsetof(PlanHeader, pad) == kPullErrorOffset, "error word offset");
-    if (!fs && pull_umma_eligible(a, d, tc_threshold)) {
+    // the bulk-copy and tcgen05 kernels split the tile range themselves and
+    // read only the header's error word; the plan is built for them too unless
+    // the caller will not reuse it (keep_plan false), so that a later call with
+    // plan_ready = 1 that dispatches to the register-gather kernel finds it
+    const bool umma = !fs && pull_umma_eligible(a, d, tc_threshold);
+    const bool tma = !umma && !fs && pull_tma_eligible(a, d);
+    if (!plan_ready) {
+        if (keep_plan || !(umma || tma)) pull_plan(a, scratch, scratch_bytes, s);
+        else TCC_CUDA(cudaMemsetAsync(hdr, 0, sizeof(PlanHeader), s));
+    }
+    if (umma) {
         pull_umma(a, d, accumulate, &hdr->pad[0], s);
         return;
     }
-    if (!fs && pull_tma_eligible(a, d)) {
+    if (tma) {
         pull_tma(a, d, tc_threshold, accumulate, &hdr->pad[0], s);
         return;
     }

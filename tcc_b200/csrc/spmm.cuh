@@ -49,9 +49,13 @@ struct FeatureStore {
 };
 
 size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
+// Builds the pull work plan in `scratch` on stream s (what plan_ready = 1 reuses).
+void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStream_t s);
+// keep_plan = false: the caller never passes plan_ready = 1 for this scratch
+// again, so the plan is built only when the dispatched kernel reads it.
 void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int accumulate,
                void* scratch, size_t scratch_bytes, bool plan_ready, const FeatureStore* fs,
-               cudaStream_t s);
+               cudaStream_t s, bool keep_plan = true);
 
 // Bulk-copy gather pull kernel (pull_tma.cu): BCSR forward / BCSC transposed over
 // a dense X; F a multiple of 4 and either <= 128 or a multiple of 128.

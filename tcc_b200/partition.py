@@ -208,5 +208,6 @@ class DistGraph:
                                 rs=self.rs, cs=self.cs_halo, accumulate=True)
         return Y
 
-    # A symmetric (every BASELINE graph): Aᵀ·G on the same partition is A·G.
+    # For a symmetric A (the GCN-normalised graphs) Aᵀ·G on the same partition
+    # is A·G.
     spmm_t = spmm

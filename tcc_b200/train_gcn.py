@@ -155,7 +155,12 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
         columns=R["tiles_g"].sparseIdx, force_gather=bool(cfg.get("cold_stage_gather", False)))
     if staged:
         side = torch.cuda.Stream(device=device)
+        # the staging buffer and its row ids were made on the current stream
+        # (the ids by an asynchronous gather): the side stream starts after them
+        side.wait_stream(torch.cuda.current_stream())
         store.cold_stage.record_stream(side)  # written on the side stream
+        if store.stage_ids is not None:
+            store.stage_ids.record_stream(side)  # read on the side stream
         ready = torch.cuda.Event()
         used = torch.cuda.Event()
         store.stage_cold(side)

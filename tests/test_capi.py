@@ -65,3 +65,15 @@ def test_reference_build_exports_harness():
     L = C.CDLL(path)
     for n in ("ref_swtcf_convert", "ref_swtcf_spmm", "ref_cnic_spmm"):
         assert hasattr(L, n)
+
+
+def test_wait_limit_setting_round_trips_without_a_gpu(lib):
+    from tcc_b200 import _lib
+    assert lib.tcc_get_wait_limit_ns() == _lib.DEFAULT_WAIT_LIMIT_NS
+    try:
+        lib.tcc_set_wait_limit_ns(12345)
+        assert lib.tcc_get_wait_limit_ns() == 12345
+    finally:
+        lib.tcc_set_wait_limit_ns(0)
+    assert lib.tcc_get_wait_limit_ns() == _lib.DEFAULT_WAIT_LIMIT_NS
+    assert lib.tcc_noalloc_device_error(None, None) == 1  # NULL code: refused before any CUDA call
