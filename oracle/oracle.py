@@ -292,6 +292,10 @@ def ref_lib():
                                         u32p, u64p, u32p, u32p, u32p, u8p, u32p, u8p,
                                         C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
                                         C.POINTER(C.c_uint32)]
+        L.ref_swtcf_convert_timed.restype = C.c_int
+        L.ref_swtcf_convert_timed.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                              u32p, u32p, C.c_int, C.c_int,
+                                              C.POINTER(C.c_float)]
         L.ref_swtcf_spmm.restype = C.c_int
         L.ref_swtcf_spmm.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, u32p, u32p, f32p, f32p,
                                      C.c_uint32, C.c_int, C.c_int, C.POINTER(C.c_float)]
@@ -336,6 +340,17 @@ def ref_swtcf_convert(rows, cols, dst, src, S=16):
     o.update(rows=rows, cols=cols, S=S, numColWindows=W, numSuperWindows=SW, T=T, R=R,
              device_error=err.value)
     return o
+
+
+def ref_swtcf_convert_ms(rows, cols, dst, src, S=16, warmup=1, reps=5):
+    """Mean ms per reference convertCOOToSWTCF call on the GPU (inputs resident)."""
+    L = ref_lib()
+    ms = C.c_float(0.0)
+    rc = L.ref_swtcf_convert_timed(rows, cols, S, len(dst), np.ascontiguousarray(dst, np.uint32),
+                                   np.ascontiguousarray(src, np.uint32), warmup, reps, C.byref(ms))
+    if rc != 0:
+        raise OracleError(rc, L.ref_last_error().decode())
+    return ms.value
 
 
 def ref_swtcf_spmm(rows, cols, dst, src, X128, tc_threshold=12, warmup=0, reps=0):

@@ -96,6 +96,51 @@ int ref_swtcf_convert(uint32_t rows, uint32_t cols, uint32_t S, uint32_t nnz,
     return rc;
 }
 
+// The reference converter's own throughput instrument
+// (src/swtcf_convert_main.cu:376-417): COO uploaded and matrix + workspace
+// allocated once, then `warmup` untimed and `reps` timed convertCOOToSWTCF calls
+// on the default stream between CUDA events; *ms_per_call = mean.
+int ref_swtcf_convert_timed(uint32_t rows, uint32_t cols, uint32_t S, uint32_t nnz,
+                            const uint32_t* dst, const uint32_t* src, int warmup, int reps,
+                            float* ms_per_call) {
+    g_msg[0] = 0;
+    DeviceSWTCFMatrix m;
+    SWTCFConvertWorkspace ws;
+    uint32_t* d_dst = nullptr;
+    uint32_t* d_src = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = 0;
+    try {
+        H_CHECK(cudaMalloc(&d_dst, sizeof(uint32_t) * nnz));
+        H_CHECK(cudaMalloc(&d_src, sizeof(uint32_t) * nnz));
+        H_CHECK(cudaMemcpy(d_dst, dst, sizeof(uint32_t) * nnz, cudaMemcpyHostToDevice));
+        H_CHECK(cudaMemcpy(d_src, src, sizeof(uint32_t) * nnz, cudaMemcpyHostToDevice));
+        allocateDeviceSWTCF(m, rows, cols, nnz, S);
+        allocateSWTCFConvertWorkspace(ws, nnz, cols, S);
+        for (int i = 0; i < warmup; ++i) convertCOOToSWTCF(d_dst, d_src, nnz, m, ws, 0);
+        H_CHECK(cudaDeviceSynchronize());
+        H_CHECK(cudaEventCreate(&e0));
+        H_CHECK(cudaEventCreate(&e1));
+        H_CHECK(cudaEventRecord(e0));
+        for (int i = 0; i < reps; ++i) convertCOOToSWTCF(d_dst, d_src, nnz, m, ws, 0);
+        H_CHECK(cudaEventRecord(e1));
+        H_CHECK(cudaEventSynchronize(e1));
+        float ms = 0.f;
+        H_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+        *ms_per_call = reps > 0 ? ms / reps : 0.f;
+    } catch (const std::exception& e) {
+        if (!g_msg[0]) fail(e.what());
+        rc = -1;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    freeSWTCFConvertWorkspace(ws);
+    freeDeviceSWTCF(m);
+    cudaFree(d_dst);
+    cudaFree(d_src);
+    return rc;
+}
+
 // Reference converter + reference SpMM (F = 128 fixed, src/swtcf_spmm.cu) on
 // one COO: Y (rows x 128, zeroed here) = pattern(A) * X (cols x 128).
 // If ms_per_launch is non-NULL the SpMM is also timed: `warmup` untimed and

@@ -38,9 +38,17 @@ class FeatureStore:
     host part.  ``hot_fraction`` of the nodes (highest degree first) go to HBM."""
 
     def __init__(self, X: np.ndarray, degrees: np.ndarray, hot_fraction: float = 0.2,
-                 device=None, col_scale: np.ndarray | None = None):
+                 device=None, col_scale: np.ndarray | None = None, shards: int = 1,
+                 shard_devices=None):
         """col_scale (optional): a per-node scale folded into the stored rows once,
-        so an aggregation over the store computes A·diag(col_scale)·X."""
+        so an aggregation over the store computes A·diag(col_scale)·X.
+
+        shards: the hot rows are split into this many GPU shards of
+        ``capacity`` rows each, hot row g in shard g // capacity at row
+        g % capacity -- the reference's per-GPU feature caches
+        (cnic/src/core/spmm_kernel.cu:145-147).  shard_devices: the device of
+        each shard (default: all on ``device``); shards on other GPUs are read
+        over NVLink with peer access, which the caller enables."""
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
         X = np.ascontiguousarray(X, dtype=np.float32)
         if col_scale is not None:
@@ -55,20 +63,32 @@ class FeatureStore:
         is_hot[hot] = True
         cold = np.nonzero(~is_hot)[0]
         self.num_nodes, self.F = n, F
-        self.capacity = max(n_hot, 1)
+        shards = max(1, min(int(shards), max(n_hot, 1)))
+        self.capacity = max((n_hot + shards - 1) // shards, 1)
         csm = np.full(n, -1, dtype=np.int32)
         csm[hot] = np.arange(n_hot, dtype=np.int32)
         idm = np.full(n, -1, dtype=np.int32)
         idm[cold] = np.arange(cold.size, dtype=np.int32)
         self.cache_search_map = torch.from_numpy(csm).to(device)
         self.id_map = torch.from_numpy(idm).to(device)
-        self.gpu_rows = torch.from_numpy(X[hot]).to(device) if n_hot else \
-            torch.zeros((1, F), dtype=torch.float32, device=device)
+        devs = list(shard_devices) if shard_devices is not None else [device] * shards
+        if len(devs) != shards:
+            raise ValueError("one device per shard")
+        hot_rows = X[hot] if n_hot else np.zeros((1, F), np.float32)
+        self.gpu_shards = [torch.from_numpy(hot_rows[k * self.capacity:(k + 1) * self.capacity])
+                           .to(devs[k]) for k in range(shards)]
         self.cpu_rows = torch.from_numpy(X[cold] if cold.size else np.zeros((1, F), np.float32)) \
             .pin_memory()
-        # device array of per-GPU shard base pointers (one shard on one GPU here)
-        self.gpu_ptrs = torch.tensor([self.gpu_rows.data_ptr()], dtype=torch.int64, device=device)
+        # device array of the shards' base pointers, indexed by g // capacity
+        self.gpu_ptrs = torch.tensor([t.data_ptr() for t in self.gpu_shards], dtype=torch.int64,
+                                     device=device)
+        self.device = torch.device(device)
         self.n_hot, self.n_cold = n_hot, int(cold.size)
+
+    @property
+    def gpu_rows(self) -> torch.Tensor:
+        """The first hot-row shard (the whole hot block when there is one)."""
+        return self.gpu_shards[0]
 
     def enable_cold_staging(self, budget_bytes: int | None = None, columns: torch.Tensor | None = None,
                             force_gather: bool = False) -> bool:
@@ -84,7 +104,7 @@ class FeatureStore:
         Returns whether staging is on."""
         if self.n_cold == 0:
             return False
-        device = self.gpu_rows.device
+        device = self.device
         ids = stage_map = None
         if columns is not None:
             c, ids, stage_map = cold_stage_plan(columns.to(device), self.cache_search_map, self.id_map,
@@ -136,10 +156,11 @@ class FeatureStore:
 
     def dense(self) -> torch.Tensor:
         """All rows gathered into one HBM tensor (for checking)."""
-        out = torch.empty((self.num_nodes, self.F), dtype=torch.float32,
-                          device=self.gpu_rows.device)
+        out = torch.empty((self.num_nodes, self.F), dtype=torch.float32, device=self.device)
         hot = self.cache_search_map >= 0
-        out[hot] = self.gpu_rows[self.cache_search_map[hot].long()]
+        g = self.cache_search_map[hot].long()
+        rows = torch.cat([t.to(self.device) for t in self.gpu_shards])
+        out[hot] = rows[g]
         cold = ~hot
         out[cold] = self.cpu_rows.to(out.device)[self.id_map[cold].long()]
         return out

@@ -144,7 +144,7 @@ class TiledGraph:
         import ctypes as C
         from . import _lib as L
         F = store.F
-        out = torch.empty((self.n, F), dtype=torch.float32, device=store.gpu_rows.device)
+        out = torch.empty((self.n, F), dtype=torch.float32, device=store.device)
         W = self.bcsr.num_windows
         full = torch.empty(((W + 1) * 8, F), dtype=torch.float32, device=out.device)
         sc = self.bcsr.scratch()

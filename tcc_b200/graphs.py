@@ -301,3 +301,53 @@ def rmat_gpu(scale: int, edges: int, seed: int, device, row_range=None,
     rowptr = torch.zeros(r1 - r0 + 1, dtype=torch.int64, device=device)
     rowptr[1:] = torch.cumsum(counts, 0)
     return rowptr, col, deg
+
+
+def sbm_gpu(n: int, blocks: int, total_edges: int, ratio: float, sigma: float, seed: int,
+            device, chunk: int = 1 << 25):
+    """``sbm`` on the GPU with torch's seeded generator (config 3 at full size in
+    seconds): degree-corrected SBM over contiguous equal blocks, intra/inter
+    pair-probability ratio ``ratio``, log-normal(sigma) propensities,
+    ~total_edges edges after symmetrisation, deduplicated, self-loops added.
+    Returns (rowptr int64 [n+1], col int32 [nnz])."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    block = (torch.arange(n, dtype=torch.int64, device=device) * blocks) // n
+    sizes = torch.bincount(block, minlength=blocks).to(torch.float64)
+    starts = torch.zeros(blocks + 1, dtype=torch.int64, device=device)
+    starts[1:] = torch.cumsum(sizes, 0).to(torch.int64)
+    prop = torch.exp(sigma * torch.randn(n, generator=gen, device=device, dtype=torch.float64))
+    share = float(torch.sum((sizes / n) ** 2))
+    p_intra = ratio * share / (ratio * share + (1.0 - share))
+    cdf = torch.cumsum(prop, 0)
+    cdf /= cdf[-1].clone()
+    m = total_edges // 2
+    keys = []
+    for s0 in range(0, m, chunk):
+        k = min(chunk, m - s0)
+        u = torch.searchsorted(cdf, torch.rand(k, generator=gen, device=device, dtype=torch.float64))
+        u = u.clamp_(max=n - 1)
+        intra = torch.rand(k, generator=gen, device=device) < p_intra
+        v = torch.searchsorted(cdf, torch.rand(k, generator=gen, device=device, dtype=torch.float64))
+        bu = block[u[intra]]
+        lo, hi = starts[bu], starts[bu + 1]
+        clo = torch.where(lo > 0, cdf[(lo - 1).clamp(min=0)], torch.zeros_like(lo, dtype=torch.float64))
+        chi = cdf[hi - 1]
+        r = clo + torch.rand(bu.numel(), generator=gen, device=device, dtype=torch.float64) * (chi - clo)
+        vi = torch.searchsorted(cdf, r)
+        v[intra] = torch.minimum(torch.maximum(vi, lo), hi - 1)
+        v = v.clamp_(max=n - 1)
+        keep = u != v
+        u, v = u[keep], v[keep]
+        keys.append((u << 32) | v)
+        keys.append((v << 32) | u)
+    diag = torch.arange(n, dtype=torch.int64, device=device)
+    keys.append((diag << 32) | diag)
+    keys = torch.unique(torch.cat(keys))
+    rows = keys >> 32
+    col = (keys & 0xFFFFFFFF).to(torch.int32)
+    counts = torch.bincount(rows, minlength=n)
+    rowptr = torch.zeros(n + 1, dtype=torch.int64, device=device)
+    rowptr[1:] = torch.cumsum(counts, 0)
+    return rowptr, col

@@ -44,6 +44,12 @@ def gather_rows(X: torch.Tensor, idx: torch.Tensor, out: torch.Tensor, stream=No
     return out
 
 
+def _event(stream):
+    e = torch.cuda.Event(enable_timing=True)
+    e.record(stream)
+    return e
+
+
 def nccl_options():
     """ProcessGroupNCCL options with high-priority NCCL streams (the halo
     exchange then overlaps the local tiles instead of queueing behind them)."""
@@ -127,6 +133,7 @@ class DistGraph:
         self.tc_threshold = tc_threshold
         self._bufs = {}
         self._side = None
+        self._tstream = None
         self.comm_sms = 32  # SMs left to the exchange during the local tiles (measured best of 0-32)
         self.tiles_loc = self.tiles_halo = None
         if build_tiles:
@@ -157,13 +164,16 @@ class DistGraph:
             self._bufs[key] = b
         return b
 
-    def exchange(self, X_local: torch.Tensor, async_op: bool = True):
+    def exchange(self, X_local: torch.Tensor, async_op: bool = True, tag: int = 0,
+                 timer: dict | None = None):
         """Start the halo exchange; returns (halo buffer, work handle or None).
-        The halo buffer is reused by the next exchange of the same width."""
-        recv = self._buf("recv", self.halo_rows, X_local)
+        The halo buffer (one per ``tag`` and width) is reused by the next
+        exchange with the same tag.  ``timer``: a dict that receives CUDA
+        events "pack{tag}" (rows packed) and "xchg{tag}" (halo arrived)."""
+        recv = self._buf(f"recv{tag}", self.halo_rows, X_local)
         if self.world == 1:
             return recv, None
-        send = self._buf("send", self.send_idx.numel(), X_local)
+        send = self._buf(f"send{tag}", self.send_idx.numel(), X_local)
         if not X_local.is_cuda:
             torch.index_select(X_local, 0, self.send_idx, out=send)
             work = dist.all_to_all_single(recv, send, self.recv_counts, self.send_counts,
@@ -175,39 +185,112 @@ class DistGraph:
         side.wait_stream(torch.cuda.current_stream(X_local.device))
         with torch.cuda.stream(side):
             gather_rows(X_local, self.send_idx, send, stream=side)
+            if timer is not None:
+                timer[f"pack{tag}"] = _event(side)
             work = dist.all_to_all_single(recv, send, self.recv_counts, self.send_counts,
                                           group=self.group, async_op=True)
+        if timer is not None:  # the arrival, seen from a stream nothing else waits on
+            if self._tstream is None:
+                self._tstream = torch.cuda.Stream(device=X_local.device)
+            with torch.cuda.stream(self._tstream):
+                work.wait()
+                timer[f"xchg{tag}"] = _event(self._tstream)
         if not async_op:
             work.wait()
             work = None
         return recv, work
 
-    def spmm(self, X_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Y[P_g] = (diag(rs) A diag(cs) X)[P_g], exchange overlapped with the
-        local-column tiles."""
+    def _local(self, X_local, out, reserve):
         from . import tiles
         from . import _lib as L
-        X_local = X_local.contiguous()
-        with torch.cuda.nvtx.range("tcc.halo_exchange_start"):
-            halo, work = self.exchange(X_local)
-        # leave SMs for the exchange's NCCL kernels while the local tiles run
-        reserve = self.comm_sms if work is not None else 0
+        # leave SMs for the exchange's NCCL kernels while these tiles run
         prev = L.lib().tcc_get_grid_reserve()
-        L.lib().tcc_set_grid_reserve(reserve)
+        L.lib().tcc_set_grid_reserve(self.comm_sms if reserve else 0)
         try:
             with torch.cuda.nvtx.range("tcc.local_tiles"):
-                Y = tiles.bcsr_spmm(self.tiles_loc, X_local, out, tc_threshold=self.tc_threshold,
-                                    rs=self.rs, cs=self.cs_local)
+                return tiles.bcsr_spmm(self.tiles_loc, X_local, out, tc_threshold=self.tc_threshold,
+                                       rs=self.rs, cs=self.cs_local)
         finally:
             L.lib().tcc_set_grid_reserve(prev)
+
+    def _halo(self, halo, work, Y, reserve=False):
+        from . import tiles
+        from . import _lib as L
         if work is not None:
             work.wait()
-        if self.tiles_halo is not None:
+        if self.tiles_halo is None:
+            return
+        prev = L.lib().tcc_get_grid_reserve()
+        L.lib().tcc_set_grid_reserve(self.comm_sms if reserve else 0)
+        try:
             with torch.cuda.nvtx.range("tcc.halo_tiles"):
                 tiles.bcsr_spmm(self.tiles_halo, halo, Y, tc_threshold=self.tc_threshold,
                                 rs=self.rs, cs=self.cs_halo, accumulate=True)
+        finally:
+            L.lib().tcc_set_grid_reserve(prev)
+
+    def spmm(self, X_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Y[P_g] = (diag(rs) A diag(cs) X)[P_g], exchange overlapped with the
+        local-column tiles."""
+        X_local = X_local.contiguous()
+        with torch.cuda.nvtx.range("tcc.halo_exchange_start"):
+            halo, work = self.exchange(X_local)
+        Y = self._local(X_local, out, reserve=work is not None)
+        self._halo(halo, work, Y)
         return Y
+
+    def spmm_pair(self, X_local: torch.Tensor, Y: torch.Tensor, G_local: torch.Tensor,
+                  Z: torch.Tensor, timer: dict | None = None):
+        """Two SpMMs over the partition, Y = Â[P_g, :]·X and Z = Â[P_g, :]·G,
+        with both halo exchanges queued back to back at the start, so G's halo
+        travels while X's tiles run.  ``timer``: a dict that receives CUDA
+        events -- "start", "pack0/1", "xchg0/1" (halos arrived), "local0/1"
+        (local tiles done) and "done0/1" (Y, Z complete)."""
+        main = torch.cuda.current_stream(X_local.device)
+        if timer is not None:
+            timer["start"] = _event(main)
+        with torch.cuda.nvtx.range("tcc.halo_exchange_start"):
+            hx, wx = self.exchange(X_local, tag=0, timer=timer)
+            hg, wg = self.exchange(G_local, tag=1, timer=timer)
+        comm = wx is not None
+        self._local(X_local, Y, reserve=comm)
+        if timer is not None:
+            timer["local0"] = _event(main)
+        self._halo(hx, wx, Y, reserve=comm)  # G's rows are still on the wire
+        if timer is not None:
+            timer["done0"] = _event(main)
+        self._local(G_local, Z, reserve=comm)
+        if timer is not None:
+            timer["local1"] = _event(main)
+        self._halo(hg, wg, Z)
+        if timer is not None:
+            timer["done1"] = _event(main)
+        return Y, Z
 
     # For a symmetric A (the GCN-normalised graphs) Aᵀ·G on the same partition
     # is A·G.
     spmm_t = spmm
+
+
+def tile_balanced_bounds(window_offset: torch.Tensor, num_rows: int, parts: int,
+                         window_cost: float = 2.0) -> list:
+    """Contiguous row bounds, on window boundaries (multiples of 8), with about
+    equal pull-kernel work per part: an 8-row window costs its tile count
+    (``window_offset``, the BCSR rowWindowOffset of the whole graph) plus
+    ``window_cost`` tiles' worth of per-window work.  Power-law graphs put
+    their hub rows, whose windows hold many tiles per nonzero less than the
+    tail's, at one end, so balancing nonzeros leaves the tail ranks slower."""
+    off = window_offset.to(torch.int64)
+    cost = torch.diff(off).to(torch.float64) + window_cost
+    cum = torch.cumsum(cost, 0)
+    total = float(cum[-1])
+    W = cost.numel()
+    cuts = []
+    for k in range(1, parts):
+        w = int(torch.searchsorted(cum, torch.tensor(total * k / parts, dtype=torch.float64,
+                                                     device=cum.device)).item())
+        cuts.append(min(num_rows, 8 * min(w + 1, W)))
+    b = [0] + cuts + [num_rows]
+    for k in range(1, len(b)):  # keep every part non-empty where rows allow
+        b[k] = max(b[k], min(num_rows, b[k - 1] + 8))
+    return b

@@ -192,9 +192,9 @@ def test_bcsc_push_and_transposed(gpu, oracle, pull_kernel, name, g, F, thr):
 def test_full_size_properties(gpu):
     """Config-2 size: A.1 = degree exactly (pattern-only, fp32 exact integers),
     linearity, and <A X, G> = <X, A^T G>."""
-    c = G.config(2)
-    g = c["graph"]
-    rp, col = csr_dev(g)
+    rp, col, _ = G.rmat_gpu(20, 16 << 20, seed=1, device="cuda")  # the bench's config-2 graph
+    g = G.Csr(rp.numel() - 1, rp.numel() - 1, rp.cpu().numpy().astype(np.uint64),
+              col.cpu().numpy().view(np.uint32))
     bcsr = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
     bcsc = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsc")
     ones = torch.ones((g.cols, 128), device="cuda")
