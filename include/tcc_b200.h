@@ -233,7 +233,8 @@ uint32_t tcc_get_grid_reserve(void);
  * word (tcc_pull_device_error), waits for its own copies still in flight and
  * returns, leaving the context usable.  Process-wide; applies to launches made
  * after the call; 0 restores the default.  Limits below 200 us poll the
- * barrier without suspending. */
+ * barrier without suspending; limits below 1 us make every wait a single test
+ * of the barrier (a wait whose copy has not landed gives up at once). */
 #define TCC_DEFAULT_WAIT_LIMIT_NS 2000000000ull
 void tcc_set_wait_limit_ns(uint64_t ns);
 uint64_t tcc_get_wait_limit_ns(void);

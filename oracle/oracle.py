@@ -296,6 +296,10 @@ def ref_lib():
         L.ref_swtcf_convert_timed.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                               u32p, u32p, C.c_int, C.c_int,
                                               C.POINTER(C.c_float)]
+        L.ref_swtcf_spmm_tiles.restype = C.c_int
+        L.ref_swtcf_spmm_tiles.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                           C.c_uint32, u32p, u64p, u32p, u32p, u32p, u8p, u32p,
+                                           u8p, f32p, f32p, C.c_uint32]
         L.ref_swtcf_spmm.restype = C.c_int
         L.ref_swtcf_spmm.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, u32p, u32p, f32p, f32p,
                                      C.c_uint32, C.c_int, C.c_int, C.POINTER(C.c_float)]
@@ -351,6 +355,22 @@ def ref_swtcf_convert_ms(rows, cols, dst, src, S=16, warmup=1, reps=5):
     if rc != 0:
         raise OracleError(rc, L.ref_last_error().decode())
     return ms.value
+
+
+def ref_swtcf_spmm_tiles(m, X128, tc_threshold=12):
+    """Reference launchSWTCFSpMM on the given SWTCF dict (e.g. the oracle's
+    canonical tiling); returns Y (rows x 128)."""
+    L = ref_lib()
+    Y = np.zeros((m["rows"], 128), np.float32)
+    rc = L.ref_swtcf_spmm_tiles(
+        m["rows"], m["cols"], m["S"], m["T"], m["R"], m["colWindowOffset"],
+        np.ascontiguousarray(m["tileLocalBit"]), np.ascontiguousarray(m["tileRowSlot"]),
+        m["superWindowRowOffset"], np.ascontiguousarray(m["superWindowRows"]),
+        np.ascontiguousarray(m["superWindowRowCacheSlot"]), m["superWindowCachedRowSlot"],
+        m["superWindowCachedCount"], np.ascontiguousarray(X128, np.float32), Y, tc_threshold)
+    if rc != 0:
+        raise OracleError(rc, L.ref_last_error().decode())
+    return Y
 
 
 def ref_swtcf_spmm(rows, cols, dst, src, X128, tc_threshold=12, warmup=0, reps=0):

@@ -141,6 +141,53 @@ int ref_swtcf_convert_timed(uint32_t rows, uint32_t cols, uint32_t S, uint32_t n
     return rc;
 }
 
+// The reference launchSWTCFSpMM on a GIVEN SWTCF tiling (e.g. the canonical
+// form), so that its arithmetic can be compared with the oracle's on the same
+// tiles: the arrays are uploaded into a reference-allocated DeviceSWTCFMatrix
+// (capacity max(T, R)), Y (rows x 128) is zeroed, Y = pattern(A) * X.
+int ref_swtcf_spmm_tiles(uint32_t rows, uint32_t cols, uint32_t S, uint32_t T, uint32_t R,
+                         const uint32_t* colWindowOffset, const uint64_t* tileLocalBit,
+                         const uint32_t* tileRowSlot, const uint32_t* superWindowRowOffset,
+                         const uint32_t* superWindowRows, const uint8_t* superWindowRowCacheSlot,
+                         const uint32_t* superWindowCachedRowSlot,
+                         const uint8_t* superWindowCachedCount, const float* X, float* Y,
+                         uint32_t tc_threshold) {
+    g_msg[0] = 0;
+    DeviceSWTCFMatrix m;
+    float* d_x = nullptr;
+    float* d_y = nullptr;
+    int rc = 0;
+    auto up = [](auto* dst, const auto* src, std::size_t n) {
+        if (n) H_CHECK(cudaMemcpy(dst, src, n * sizeof(*src), cudaMemcpyHostToDevice));
+    };
+    try {
+        allocateDeviceSWTCF(m, rows, cols, T > R ? (T ? T : 1) : (R ? R : 1), S);
+        const uint32_t W = m.numColWindows, SW = m.numSuperWindows;
+        up(m.colWindowOffset, colWindowOffset, W + 1);
+        up(m.tileLocalBit, tileLocalBit, T);
+        up(m.tileRowSlot, tileRowSlot, (std::size_t)T * 8);
+        up(m.superWindowRowOffset, superWindowRowOffset, SW + 1);
+        up(m.superWindowRows, superWindowRows, R);
+        up(m.superWindowRowCacheSlot, superWindowRowCacheSlot, R);
+        up(m.superWindowCachedRowSlot, superWindowCachedRowSlot, (std::size_t)SW * 32);
+        up(m.superWindowCachedCount, superWindowCachedCount, SW);
+        H_CHECK(cudaMalloc(&d_x, sizeof(float) * (std::size_t)cols * 128));
+        H_CHECK(cudaMalloc(&d_y, sizeof(float) * (std::size_t)rows * 128));
+        H_CHECK(cudaMemcpy(d_x, X, sizeof(float) * (std::size_t)cols * 128, cudaMemcpyHostToDevice));
+        H_CHECK(cudaMemset(d_y, 0, sizeof(float) * (std::size_t)rows * 128));
+        launchSWTCFSpMM(m, d_x, d_y, tc_threshold, 0);
+        H_CHECK(cudaDeviceSynchronize());
+        download(Y, d_y, (std::size_t)rows * 128);
+    } catch (const std::exception& e) {
+        if (!g_msg[0]) fail(e.what());
+        rc = -1;
+    }
+    freeDeviceSWTCF(m);
+    cudaFree(d_x);
+    cudaFree(d_y);
+    return rc;
+}
+
 // Reference converter + reference SpMM (F = 128 fixed, src/swtcf_spmm.cu) on
 // one COO: Y (rows x 128, zeroed here) = pattern(A) * X (cols x 128).
 // If ms_per_launch is non-NULL the SpMM is also timed: `warmup` untimed and

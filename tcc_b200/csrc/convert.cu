@@ -46,29 +46,29 @@ __global__ void keys_from_coo_kernel(const uint32_t* __restrict__ dst,
 }
 
 // CSR -> keys.  mode 0: window = row (BCSR); mode 1: window = col (BCSC, SWTCF).
+// One warp per row, its lanes striding over the row's nonzeros (coalesced).
 __global__ void keys_from_csr_kernel(const uint64_t* __restrict__ rowptr,
                                      const uint32_t* __restrict__ col, uint32_t rows,
                                      uint32_t cols, uint64_t n, int mode, int ybits,
                                      uint64_t* __restrict__ keys, uint32_t* __restrict__ vals,
                                      uint32_t* err) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    // row = largest r with rowptr[r] <= i
-    uint32_t lo = 0, hi = rows;
-    while (lo < hi) {
-        const uint32_t mid = lo + (hi - lo + 1) / 2;
-        if (rowptr[mid] <= i) lo = mid; else hi = mid - 1;
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+        // the last row also takes any entries past rowptr[rows] (as before)
+        const uint64_t b = rowptr[r], e = r + 1 == rows ? n : min(rowptr[r + 1], n);
+        for (uint64_t i = b + lane; i < e; i += 32) {
+            uint32_t c = col[i];
+            if (c >= cols) {
+                raise_error(err, TCC_DEVERR_INDEX_RANGE);
+                c = 0;
+            }
+            const uint32_t x = mode == 0 ? (uint32_t)r : c;
+            const uint32_t y = mode == 0 ? c : (uint32_t)r;
+            keys[i] = ((uint64_t)(x >> 3) << ybits) | y;
+            vals[i] = x & 7u;
+        }
     }
-    uint32_t r = lo < rows ? lo : rows - 1;
-    uint32_t c = col[i];
-    if (c >= cols) {
-        raise_error(err, TCC_DEVERR_INDEX_RANGE);
-        c = 0;
-    }
-    const uint32_t x = mode == 0 ? r : c;
-    const uint32_t y = mode == 0 ? c : r;
-    keys[i] = ((uint64_t)(x >> 3) << ybits) | y;
-    vals[i] = x & 7u;
 }
 
 // SWTCF tile t of column window w (the largest w with col_off[w] <= t): each
@@ -270,17 +270,31 @@ __global__ void superwindow_rows_kernel(const uint64_t* __restrict__ keys,
                                         const uint32_t* __restrict__ head,
                                         const uint32_t* __restrict__ excl,
                                         const uint32_t* __restrict__ d_ng, int ybits,
-                                        uint32_t SW, uint32_t* __restrict__ rows_out,
+                                        uint32_t* __restrict__ rows_out,
                                         uint32_t* __restrict__ rstart,
-                                        uint32_t* __restrict__ swcnt) {
+                                        uint32_t* __restrict__ rsw) {
     const uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= *d_ng || !head[q]) return;
     const uint32_t r = excl[q];
     const uint64_t key = keys[q];
     rows_out[r] = (uint32_t)(key & ((1ull << ybits) - 1));
     rstart[r] = (uint32_t)q;
-    const uint32_t s = (uint32_t)(key >> ybits);
-    if (s < SW) atomicAdd(&swcnt[s], 1u);
+    rsw[r] = (uint32_t)(key >> ybits);
+}
+
+// superWindowRowOffset[s] = number of unique rows of super-windows < s: the
+// rows are sorted by super-window, so it is a lower bound in rsw[0, R).
+__global__ void superwindow_offsets_kernel(const uint32_t* __restrict__ rsw,
+                                           const uint32_t* __restrict__ d_R, uint32_t SW,
+                                           uint32_t* __restrict__ swo) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s > SW) return;
+    uint32_t lo = 0, hi = *d_R;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo) / 2;
+        if (rsw[mid] < s) lo = mid + 1; else hi = mid;
+    }
+    swo[s] = lo;
 }
 
 __global__ void superwindow_slots_kernel(const uint64_t* __restrict__ keys,
@@ -394,6 +408,11 @@ __global__ void __launch_bounds__(kThreads) repeat_cache_kernel(
 }
 
 inline unsigned blocks(uint64_t n) { return (unsigned)((n + kThreads - 1) / kThreads); }
+// keys_from_csr_kernel: a warp per row, grid-stride over rows
+inline unsigned csr_blocks(uint64_t rows) {
+    const uint64_t want = (rows + kThreads / 32 - 1) / (kThreads / 32);
+    return (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(want, (uint64_t)sm_count() * 64));
+}
 
 }  // namespace
 
@@ -430,10 +449,14 @@ static GroupBuffers take_groups(Arena& a, uint64_t E) {
 // Steps 2-4: sort the keys already in (keys, vals), build groups, count them
 // per window and scan: wgstart[W+1] (groups before each window) and
 // off[W+1] (tiles before each window; off[W] = T).  small[1] = groups.
+// y_sorted: the keys arrive in nondecreasing y (keys built from a CSR with
+// the window on the column side), so a stable sort of the window bits alone
+// gives (window, y) order and the y digits are skipped.
 static void build_windows(GroupBuffers& b, uint64_t n, int key_bits, int ybits, uint32_t W,
                           uint32_t* wcnt, uint32_t* wgstart, uint32_t* tiles, uint32_t* off,
-                          uint32_t* small, void* tmp, cudaStream_t s) {
-    if (radix_sort_pairs(b.keys, b.vals, b.keys_alt, b.vals_alt, n, key_bits, tmp, s)) {
+                          uint32_t* small, void* tmp, cudaStream_t s, bool y_sorted = false) {
+    if (radix_sort_pairs(b.keys, b.vals, b.keys_alt, b.vals_alt, n, key_bits, tmp, s,
+                         y_sorted ? ybits : 0)) {
         std::swap(b.keys, b.keys_alt);
         std::swap(b.vals, b.vals_alt);
     }
@@ -510,12 +533,11 @@ void swtcf_convert(const uint32_t* d_dst, const uint32_t* d_src, const uint64_t*
         keys_from_coo_kernel<<<blocks(nnz), kThreads, 0, s>>>(d_dst, d_src, nnz, m->rows, m->cols,
                                                              ybits, b.keys, b.vals, ws.small);
     } else {
-        keys_from_csr_kernel<<<blocks(nnz), kThreads, 0, s>>>(d_rowptr, d_col, m->rows, m->cols,
-                                                             nnz, 1, ybits, b.keys, b.vals,
-                                                             ws.small);
+        keys_from_csr_kernel<<<csr_blocks(m->rows), kThreads, 0, s>>>(
+            d_rowptr, d_col, m->rows, m->cols, nnz, 1, ybits, b.keys, b.vals, ws.small);
     }
     build_windows(b, nnz, wbits + ybits, ybits, W, ws.wcnt, ws.wgstart, ws.tiles,
-                  m->colWindowOffset, ws.small, ws.tmp, s);
+                  m->colWindowOffset, ws.small, ws.tmp, s, /*y_sorted=*/d_dst == nullptr);
 
     // degree-descending, dst-ascending order inside each window
     GroupBuffers d = b;  // reuse the edge sort buffers for the group sorts
@@ -537,12 +559,11 @@ void swtcf_convert(const uint32_t* d_dst, const uint32_t* d_src, const uint64_t*
     uint32_t* excl3 = b.excl;
     row_heads_kernel<<<blocks(nnz), kThreads, 0, s>>>(k3, ws.small + 1, nnz, head3);
     exclusive_scan<uint32_t>(head3, excl3, nnz, ws.small + 2, ws.tmp, s);
-    TCC_CUDA(cudaMemsetAsync(ws.swcnt, 0, (size_t)SW * 4, s));
+    // occ is free until the slots kernel: it holds each unique row's super-window
     superwindow_rows_kernel<<<blocks(nnz), kThreads, 0, s>>>(k3, head3, excl3, ws.small + 1, ybits,
-                                                             SW, m->superWindowRows, ws.rstart,
-                                                             ws.swcnt);
-    exclusive_scan<uint32_t>(ws.swcnt, m->superWindowRowOffset, SW, m->superWindowRowOffset + SW,
-                             ws.tmp, s);
+                                                             m->superWindowRows, ws.rstart, ws.occ);
+    superwindow_offsets_kernel<<<blocks((uint64_t)SW + 1), kThreads, 0, s>>>(
+        ws.occ, ws.small + 2, SW, m->superWindowRowOffset);
     superwindow_slots_kernel<<<blocks(nnz), kThreads, 0, s>>>(
         k3, v3, head3, excl3, ws.small + 1, ws.small + 2, ws.rstart, m->superWindowRowOffset,
         ybits, ws.gslot, ws.occ);
@@ -604,11 +625,11 @@ uint64_t tiles_prepare(TilesWorkspace& ws, int kind, const uint64_t* d_rowptr,
     const int wbits = std::max(1, bits_for(ws.W));
     TCC_CUDA(cudaMemsetAsync(ws.small, 0, 64, s));
     if (nnz)
-        keys_from_csr_kernel<<<blocks(nnz), kThreads, 0, s>>>(
+        keys_from_csr_kernel<<<csr_blocks(rows), kThreads, 0, s>>>(
             d_rowptr, d_col, rows, cols, nnz, kind == TCC_TILES_BCSR ? 0 : 1, ws.ybits, ws.g.keys,
             ws.g.vals, ws.small);
     build_windows(ws.g, nnz, wbits + ws.ybits, ws.ybits, ws.W, ws.wcnt, ws.wgstart, ws.tiles,
-                  ws.off, ws.small, ws.tmp, s);
+                  ws.off, ws.small, ws.tmp, s, /*y_sorted=*/kind == TCC_TILES_BCSC);
     return finish_prepare(ws, s);
 }
 

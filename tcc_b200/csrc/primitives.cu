@@ -3,8 +3,12 @@
 // These replace the CUB DeviceScan / DeviceRadixSort / DeviceRunLengthEncode
 // calls of the reference converter (src/swtcf_convert.cu:1951-2007).  The sort
 // is a classic three-kernel LSD pass (tile histograms, scan of the digit-major
-// histogram table, stable tile-local ranking + coalesced scatter); ranking uses
-// warp __match_any_sync so each pass is stable and deterministic.
+// histogram table, stable tile-local ranking + coalesced scatter).  Ranking:
+// each warp owns a contiguous run of the tile and ranks it against a
+// warp-private digit histogram (__match_any_sync groups equal digits; no
+// block barrier per item); one block-wide prefix over the warps' histograms
+// then places every warp's items after those of the warps before it, so each
+// pass is stable and deterministic.
 #include "primitives.cuh"
 
 namespace tcc {
@@ -129,11 +133,17 @@ __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(
 struct SortSmem {
     uint64_t keys[kSortTile];
     uint32_t vals[kSortTile];
-    uint32_t warp_cnt[kSortWarps][kRadix];
-    uint32_t run_cnt[kRadix];
+    uint32_t warp_cnt[kSortWarps][kRadix + 1];  // digit counts, then prefixes; [kRadix]: sentinel
     uint32_t digit_start[kRadix];
     uint32_t scan_ws[kScanThreads / 32 + 1];
 };
+
+// Warp w ranks tile items [w * kWarpItems, (w + 1) * kWarpItems), item j of
+// lane l at w * kWarpItems + j * 32 + l: the rank of an item among its warp's
+// items with the same digit is the warp's running count for that digit plus
+// the equal digits of lower lanes in the same step.
+constexpr int kWarpItems = kSortTile / kSortWarps;  // 512
+static_assert(kWarpItems == kSortItems * 32, "one warp-contiguous run per warp");
 
 __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
     const uint64_t* __restrict__ keys, const uint32_t* __restrict__ vals, uint64_t n, int shift,
@@ -145,14 +155,15 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
     const uint64_t base = (uint64_t)blockIdx.x * kSortTile;
     const uint64_t rem_n = n - base;
     const uint32_t tile_n = rem_n < (uint64_t)kSortTile ? (uint32_t)rem_n : (uint32_t)kSortTile;
-
+    for (int i = lane; i <= kRadix; i += 32) S.warp_cnt[warp][i] = 0;
+    __syncwarp();
     uint64_t k[kSortItems];
     uint32_t v[kSortItems];
     uint32_t d[kSortItems];
     uint32_t rank[kSortItems];
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
-        const uint32_t p = (uint32_t)j * kSortThreads + tid;
+        const uint32_t p = (uint32_t)(warp * kWarpItems + j * 32 + lane);
         if (p < tile_n) {
             k[j] = keys[base + p];
             v[j] = vals[base + p];
@@ -160,40 +171,36 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
         } else {
             k[j] = 0;
             v[j] = 0;
-            d[j] = kRadix;  // sentinel: never ranked or written
+            d[j] = kRadix;  // sentinel bucket: never written out
         }
     }
-    S.run_cnt[tid] = 0;
+    uint32_t* cnt = S.warp_cnt[warp];
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
-#pragma unroll
-        for (int w = 0; w < kSortWarps; ++w) S.warp_cnt[w][tid] = 0;
-        __syncthreads();
         const unsigned peers = __match_any_sync(0xffffffffu, d[j]);
-        const uint32_t lrank = __popc(peers & lanemask_lt());
-        if (d[j] < kRadix && lrank == 0) S.warp_cnt[warp][d[j]] = __popc(peers);
-        __syncthreads();
-        if (d[j] < kRadix) {
-            uint32_t r = S.run_cnt[d[j]] + lrank;
-            for (int w = 0; w < warp; ++w) r += S.warp_cnt[w][d[j]];
-            rank[j] = r;
-        }
-        __syncthreads();
-        uint32_t add = 0;
-#pragma unroll
-        for (int w = 0; w < kSortWarps; ++w) add += S.warp_cnt[w][tid];
-        S.run_cnt[tid] += add;
-        // next iteration's first barrier orders this update before its reads
+        const uint32_t before = cnt[d[j]];
+        __syncwarp();
+        if ((peers & lanemask_lt()) == 0) cnt[d[j]] = before + __popc(peers);
+        __syncwarp();
+        rank[j] = before + __popc(peers & lanemask_lt());
     }
     __syncthreads();
+    // digit t: exclusive prefix over the warps, then over the digits
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+        const uint32_t c = S.warp_cnt[w][tid];
+        S.warp_cnt[w][tid] = run;
+        run += c;
+    }
     uint32_t total;
-    const uint32_t start = block_exclusive<uint32_t>(S.run_cnt[tid], S.scan_ws, total);
+    const uint32_t start = block_exclusive<uint32_t>(run, S.scan_ws, total);
     S.digit_start[tid] = start;
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
         if (d[j] < kRadix) {
-            const uint32_t p = S.digit_start[d[j]] + rank[j];
+            const uint32_t p = S.digit_start[d[j]] + cnt[d[j]] + rank[j];
             S.keys[p] = k[j];
             S.vals[p] = v[j];
         }
@@ -246,9 +253,10 @@ size_t radix_tmp_bytes(uint64_t n) {
 }
 
 bool radix_sort_pairs(uint64_t* keys, uint32_t* vals, uint64_t* keys_alt, uint32_t* vals_alt,
-                      uint64_t n, int key_bits, void* tmp, cudaStream_t s) {
+                      uint64_t n, int key_bits, void* tmp, cudaStream_t s, int first_bit) {
     TCC_REQUIRE(n < (1ull << 31), "radix sort supports fewer than 2^31 items per call");
-    if (n <= 1 || key_bits <= 0) return false;
+    TCC_REQUIRE(first_bit >= 0, "negative first sort bit");
+    if (n <= 1 || key_bits <= first_bit) return false;
     const uint32_t tiles = (uint32_t)((n + kSortTile - 1) / kSortTile);
     uint32_t* counts = reinterpret_cast<uint32_t*>(tmp);
     const uint64_t ncounts = (uint64_t)tiles * kRadix;
@@ -262,7 +270,7 @@ bool radix_sort_pairs(uint64_t* keys, uint32_t* vals, uint64_t* keys_alt, uint32
     uint64_t* kout = keys_alt;
     uint32_t* vout = vals_alt;
     bool in_alt = false;
-    for (int shift = 0; shift < key_bits; shift += 8) {
+    for (int shift = first_bit; shift < key_bits; shift += 8) {
         radix_upsweep_kernel<<<tiles, kSortThreads, 0, s>>>(kin, n, shift, tiles, counts);
         exclusive_scan<uint32_t>(counts, counts, ncounts, nullptr, scan_tmp, s);
         radix_downsweep_kernel<<<tiles, kSortThreads, sizeof(SortSmem), s>>>(

@@ -13,15 +13,21 @@
 //   windows longer than kFlushTiles tiles (whose warp flushes every
 //   kFlushTiles tiles to keep fp32 sums short), are zeroed first and reduced
 //   with red.global.add.v4.
-// * Gathers: each real feature row of a tile (up to 8 x 512 B) is fetched by
-//   one bulk async copy (the TMA unit's cp.async.bulk) into a per-warp ring of
-//   kR shared-memory stages completed through mbarriers; the 8 rows of a tile
-//   are issued by 8 lanes in one instruction.  This keeps the row gathers off
-//   the LSU/L1 fill path, where every missed 32-byte sector costs a data-pipe
-//   wavefront (measured on B200: register gathers top out near 32 B/clk/SM
-//   from L2, bulk copies above 48).  Rows sit 32 bytes apart beyond their
-//   length, so the MMA fragment loads (4 rows x 2 float4 per quarter-warp) hit
-//   distinct banks.
+// * Gathers: the 8 feature rows of a tile (up to 8 x 512 B) are fetched by the
+//   TMA unit into a per-warp ring of kR shared-memory stages completed through
+//   mbarriers.  Default: two cp.async.bulk.tensor tile::gather4 copies per tile
+//   (rows 0-3 and 4-7, issued by two lanes in one instruction) through a 2D
+//   tensor map over X whose box is one row high and 8 floats wider than the
+//   row slice -- the extra floats (the next features, or zeros past the last
+//   feature) give the 32-byte row pitch below, and a padding column's row
+//   coordinate lies past the last row of X, so the TMA unit fills it with
+//   zeros.  TCC_PULL_COPY=bulk instead issues one cp.async.bulk per real row
+//   (8 lanes per tile) and copies a static zero row for padding.  Either way
+//   the row gathers stay off the LSU/L1 fill path, where every missed 32-byte
+//   sector costs a data-pipe wavefront (measured on B200: register gathers top
+//   out near 32 B/clk/SM from L2, TMA copies above 48).  Rows sit 32 bytes
+//   apart beyond their length, so the MMA fragment loads (4 rows x 2 float4
+//   per quarter-warp) hit distinct banks.
 // * Arithmetic: the register-gather kernel's (tile_mma): X rows scaled by the
 //   column scale in fp32, then TF32 rounded like cvt.rna for tiles with
 //   popcount >= tc_threshold (the reference's dense-tile arithmetic) and the
@@ -37,10 +43,14 @@
 #include "spmm.cuh"
 #include "tile_mma.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 namespace tcc {
 
@@ -66,6 +76,9 @@ struct __align__(16) StageMeta {
 // Source of the stage rows of padding columns: every stage row is written
 // by one copy, so padding rows hold zeros, never stale data.
 __device__ __align__(16) float g_zero_row[kMaxBox];
+static_assert(((4 * (kMaxBox * 4 + kRowPad) + 127) & ~127u) + 4 * (kMaxBox * 4 + kRowPad) <=
+                  kStageBytes && kStageBytes % 128 == 0,
+              "two 128-byte aligned halves of 4 rows fit a stage");
 static_assert(sizeof(StageMeta) == 64 && offsetof(StageMeta, cs) == 0,
               "stage metadata: 64 bytes, column scales 16-byte aligned");
 
@@ -112,8 +125,11 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 
 // Wait for phase `parity` of the mbarrier; false once limit_ns have passed.
 // Limits shorter than one suspended try poll without suspending, so that the
-// limit, not the suspend hint, decides when the wait gives up.
+// limit, not the suspend hint, decides when the wait gives up; limits below
+// the timer's resolution (kTickNs) make the wait one test of the phase.
+constexpr unsigned long long kTickNs = 1000;
 __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+    if (limit_ns < kTickNs) return mbar_test(bar, parity);
     const bool poll = limit_ns < kSuspendNs;
     if (poll ? mbar_test(bar, parity) : mbar_try(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
@@ -130,6 +146,19 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
+}
+
+// Four rows (tensor-map row coordinates r) of the box at feature column c0 into
+// consecutive box-sized pieces of shared memory at dst, completing on `bar`.
+// Row coordinates outside the tensor read as zeros.
+__device__ __forceinline__ void gather4(uint32_t dst, const CUtensorMap* tm, int32_t c0, uint4 r,
+                                        uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(r.x), "r"(r.y), "r"(r.z),
+        "r"(r.w), "r"(bar)
+        : "memory");
 }
 
 // One contiguous global -> shared copy by the TMA unit, completing on `bar`
@@ -219,10 +248,12 @@ __global__ void zero_reduced_kernel(const uint32_t* __restrict__ off, uint32_t W
 }
 
 // FULL: bw == 64 * NP (every float4 slot of the warp is a real feature).
-template <int NP, bool FULL>
+// G4: rows by tile::gather4 through `tm` (else one bulk copy per row).
+template <int NP, bool FULL, bool G4>
 __global__ void __launch_bounds__(kTW * 32, 1)
-    pull_tma_kernel(PullTiles a, Dense d, uint32_t bw, uint32_t thr, int accumulate,
-                    uint32_t* __restrict__ err, unsigned long long wait_ns) {
+    pull_tma_kernel(const __grid_constant__ CUtensorMap tm, PullTiles a, Dense d, uint32_t bw,
+                    uint32_t thr, int accumulate, uint32_t* __restrict__ err,
+                    unsigned long long wait_ns) {
     extern __shared__ unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -240,6 +271,10 @@ __global__ void __launch_bounds__(kTW * 32, 1)
 
     const uint32_t rowbytes = FULL ? 256 * NP : bw * 4;
     const uint32_t pitch = rowbytes + kRowPad;
+    // rows 0-3 of a stage at 0, pitch, 2 pitch, 3 pitch; rows 4-7 from the next
+    // 128-byte boundary (a tensor copy's shared-memory destination is 128-byte
+    // aligned); 8 x 544 bytes for a 128-float slice, which the stage size fits
+    const uint32_t half = (4 * pitch + 127u) & ~127u;
     const int32_t fb = (int32_t)(blockIdx.y * kMaxBox);
     const int gid = lane >> 2, tig = lane & 3;
     // piece p = g + j * GW of the kPieces * GW equal tile pieces; a warp's
@@ -275,6 +310,14 @@ __global__ void __launch_bounds__(kTW * 32, 1)
     };
 
     Batch B0, B1, B2;
+    // G4: row coordinates of rows (lane & ~3) .. +3 of B0 (a padding column:
+    // past the last row of X, read as zeros)
+    auto make_quad = [&]() {
+        const uint32_t v = B0.idx < a.num_in ? B0.idx : a.num_in;
+        const int q0 = lane & ~3;
+        return make_uint4(__shfl_sync(0xffffffffu, v, q0), __shfl_sync(0xffffffffu, v, q0 + 1),
+                          __shfl_sync(0xffffffffu, v, q0 + 2), __shfl_sync(0xffffffffu, v, q0 + 3));
+    };
     uint32_t mb = 0;
     uint32_t iq = 0;            // ring slot of the next issued tile
     uint32_t cq = 0, cpar = 0;  // ring slot and phase parity of the next consumed tile
@@ -291,6 +334,8 @@ __global__ void __launch_bounds__(kTW * 32, 1)
         }
         const uint32_t q = iq;
         if (++iq == (uint32_t)kR) iq = 0;
+        uint4 quad;
+        if (G4) quad = make_quad();
         if ((uint32_t)grp == t - mb) {
             const uint32_t bar = smem_u32(&sbar[q]);
             StageMeta& m = smeta[q];
@@ -299,9 +344,20 @@ __global__ void __launch_bounds__(kTW * 32, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             // the transaction count may run ahead of expect_tx (it goes
             // negative); the phase cannot complete before this arrival
-            if (krow == 0) mbar_arrive_tx(bar, 8 * rowbytes);
-            const float* row = B0.idx < a.num_in ? d.X + (uint64_t)B0.idx * d.ldx + fb : g_zero_row;
-            bulk_copy(smem_u32(sdata + q * kStageBytes) + krow * pitch, row, rowbytes, bar);
+            if (G4) {
+                // rows krow .. krow + 3 of the tile, a padding column past the
+                // last row of X (zero fill); lanes krow = 0, 4 issue
+                if (krow == 0) mbar_arrive_tx(bar, 8 * pitch);
+                if ((krow & 3) == 0)
+                    gather4(smem_u32(sdata + q * kStageBytes) + (krow >> 2) * half, &tm, fb, quad,
+                            bar);
+            } else {
+                if (krow == 0) mbar_arrive_tx(bar, 8 * rowbytes);
+                const float* row =
+                    B0.idx < a.num_in ? d.X + (uint64_t)B0.idx * d.ldx + fb : g_zero_row;
+                bulk_copy(smem_u32(sdata + q * kStageBytes) + (krow >> 2) * half + (krow & 3) * pitch,
+                          row, rowbytes, bar);
+            }
         }
     };
 
@@ -425,7 +481,7 @@ __global__ void __launch_bounds__(kTW * 32, 1)
                         const uint32_t f = 4 * (gid + 8 * sl);
                         x[r][sl] = FULL || f < bw
                                        ? f4_scale(*reinterpret_cast<const float4*>(
-                                                      src + (tig + 4 * r) * pitch + 4 * f),
+                                                      src + r * half + tig * pitch + 4 * f),
                                                   c[r])
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
@@ -476,21 +532,72 @@ bool pull_tma_eligible(const PullTiles& a, const Dense& d) {
     return d.F % 4 == 0 && (d.F <= kMaxBox || d.F % kMaxBox == 0);
 }
 
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) throw Error(TCC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+bool use_gather4() {
+    const char* e = std::getenv("TCC_PULL_COPY");
+    return !(e && std::strcmp(e, "bulk") == 0);
+}
+
+}  // namespace
+
 void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, uint32_t* err,
               cudaStream_t s) {
     const uint32_t bw = d.F <= kMaxBox ? d.F : kMaxBox;
     const uint32_t slices = d.F <= kMaxBox ? 1 : d.F / kMaxBox;
     const uint32_t ctas = (uint32_t)grid_sms();
     const uint32_t G = ctas * kTW * kPieces;
+    const bool g4 = use_gather4();
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof(tm));
+    if (g4) {
+        // rows of X as a 2D tensor [num_in][F]; box: one row, the slice plus
+        // kRowPad bytes (the stage row pitch); x = slice start, a multiple of
+        // kMaxBox floats (16-byte aligned)
+        TCC_REQUIRE(a.num_in < 0x7FFFFFFFu, "gather4 row coordinates are 32-bit signed");
+        cuuint64_t dims[2] = {d.F, a.num_in};
+        cuuint64_t strides[1] = {d.ldx * sizeof(float)};
+        cuuint32_t box[2] = {bw + kRowPad / 4, 1};
+        cuuint32_t estr[2] = {1, 1};
+        const CUresult r = tensor_map_encoder()(
+            &tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(d.X), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) throw Error(TCC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the X rows");
+    }
     if (!accumulate && a.num_tiles > 0)
         zero_reduced_kernel<<<std::min<unsigned>(ceil_div(a.num_windows, 8), ctas * 8), 256, 0, s>>>(
             a.win_offset, a.num_windows, a.num_tiles, G, d.Y, d.ldy, d.F, a.num_out);
-    auto k = bw == 128  ? pull_tma_kernel<2, true>
-             : bw == 64 ? pull_tma_kernel<1, true>
-             : bw < 64  ? pull_tma_kernel<1, false>
-                        : pull_tma_kernel<2, false>;
+    auto pick = [&](auto full_tag, auto np_tag) {
+        constexpr bool FULLv = decltype(full_tag)::value;
+        constexpr int NPv = decltype(np_tag)::value;
+        return g4 ? pull_tma_kernel<NPv, FULLv, true> : pull_tma_kernel<NPv, FULLv, false>;
+    };
+    using T = std::true_type;
+    using Fa = std::false_type;
+    using One = std::integral_constant<int, 1>;
+    using Two = std::integral_constant<int, 2>;
+    auto k = bw == 128  ? pick(T{}, Two{})
+             : bw == 64 ? pick(T{}, One{})
+             : bw < 64  ? pick(Fa{}, One{})
+                        : pick(Fa{}, Two{});
     TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(a, d, bw, thr, accumulate, err,
+    k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(tm, a, d, bw, thr, accumulate, err,
                                                        (unsigned long long)wait_limit_ns());
     TCC_CUDA(cudaGetLastError());
 }

@@ -113,19 +113,24 @@ def test_swtcf_transposed(gpu, oracle, name, g, F):
     assert rel_fro(Z2.cpu().numpy(), oracle.csr_spmm_t(g, Gm)) <= TF32_TOL
 
 
-PULL_KERNELS = ["default", "ldg", "tma", "umma"]
+PULL_KERNELS = ["default", "ldg", "tma", "tma-bulk", "umma"]
 
 
 @pytest.fixture(params=PULL_KERNELS)
 def pull_kernel(request, monkeypatch):
     """Run a pull test on each pull kernel: the default dispatch (bulk-copy
     kernel for F a multiple of 128, register-gather kernel otherwise), the
-    register-gather kernel (TCC_PULL_KERNEL=ldg), the bulk-copy gather kernel
-    (=tma) and the tcgen05 kernel (=umma; tc_threshold 0, F a multiple of
-    128).  Shapes a kernel does not take fall back to the register-gather
-    kernel."""
+    register-gather kernel (TCC_PULL_KERNEL=ldg), the TMA gather kernel (=tma)
+    with its tile::gather4 copies and with per-row bulk copies
+    (TCC_PULL_COPY=bulk), and the tcgen05 kernel (=umma; tc_threshold 0, F a
+    multiple of 128).  Shapes a kernel does not take fall back to the
+    register-gather kernel."""
+    monkeypatch.delenv("TCC_PULL_COPY", raising=False)
     if request.param == "default":
         monkeypatch.delenv("TCC_PULL_KERNEL", raising=False)
+    elif request.param == "tma-bulk":
+        monkeypatch.setenv("TCC_PULL_KERNEL", "tma")
+        monkeypatch.setenv("TCC_PULL_COPY", "bulk")
     else:
         monkeypatch.setenv("TCC_PULL_KERNEL", request.param)
     return request.param
@@ -149,20 +154,24 @@ def test_bcsr_pull(gpu, oracle, pull_kernel, name, g, F, thr):
     assert rel_fro(Y2.cpu().numpy(), 2 * want) <= (FP32_TOL if thr > 64 else TF32_TOL)
 
 
-@pytest.mark.parametrize("kernel", ["ldg", "tma", "umma"])
+@pytest.mark.parametrize("kernel", ["ldg", "tma", "tma-bulk", "umma"])
 def test_bcsr_pull_matches_tile_arithmetic(gpu, oracle, monkeypatch, kernel):
     """TF32 on every tile (tc_threshold 0) against its exact restatement: the
     register-gather and bulk-copy kernels round X like cvt.rna (the oracle's
     tile emulation); the tcgen05 kernel hands the tensor core raw fp32 bits
     and it drops the low 13 mantissa bits, i.e. A.trunc(X) summed in fp32.
     The device error word stays clear."""
-    monkeypatch.setenv("TCC_PULL_KERNEL", kernel)
+    monkeypatch.setenv("TCC_PULL_KERNEL", kernel.split("-")[0])
+    if kernel == "tma-bulk":
+        monkeypatch.setenv("TCC_PULL_COPY", "bulk")
+    else:
+        monkeypatch.delenv("TCC_PULL_COPY", raising=False)
     g = G.sbm(2000, 20, 120000, 40.0, 1.2, seed=12)
     rp, col = csr_dev(g)
     t = tiles.from_csr(rp, col, g.rows, g.cols, kind="bcsr")
     X = G.features(g.cols, 128, seed=9)
     Y = tiles.bcsr_spmm(t, dense(X), tc_threshold=0)
-    if kernel in ("ldg", "tma"):
+    if kernel in ("ldg", "tma", "tma-bulk"):
         want = oracle.bcsr_spmm(oracle.bcsr_from_csr(g), X, tc_threshold=0)
     else:
         want = oracle.csr_spmm(g, oracle.tf32_trunc(X))
