@@ -656,17 +656,29 @@ def convert_rates(rowptr, col, device, reps=5):
     E = col.numel()
     m = swtcf.SWTCFMatrix(n, n, E, 16)
     ws = swtcf.SWTCFConvertWorkspace(E, n, 16)
-    ts = []
-    for i in range(reps + 1):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        swtcf.convert_csr(rowptr, col, m, ws)
-        e1.record()
-        torch.cuda.synchronize()
-        if i:
-            ts.append(e0.elapsed_time(e1))
+    # the reference's input form: COO (dst = row, src = column), dst ascending
+    dst = torch.repeat_interleave(torch.arange(n, device=device, dtype=torch.int32),
+                                  torch.diff(rowptr))
+    src = col
+
+    def timed(fn):
+        ts = []
+        for i in range(reps + 1):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i:
+                ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    ms_coo = timed(lambda: swtcf.convert_coo(dst, src, m, ws))
+    ms = timed(lambda: swtcf.convert_csr(rowptr, col, m, ws))
+    assert ws.device_error() == 0
     ws.free()
     m.free()
+    del dst
     tw = T.TilesWorkspace(E, n, n)
     tt = []
     for i in range(reps + 1):
@@ -676,12 +688,16 @@ def convert_rates(rowptr, col, device, reps=5):
         if i:
             tt.append((time.perf_counter() - t0) * 1e3)
     tw.free()
-    ms, mt = statistics.median(ts), statistics.median(tt)
-    return {"edges": E, "swtcf_convert_csr_ms": round(ms, 3),
+    mt = statistics.median(tt)
+    return {"edges": E, "swtcf_convert_coo_ms": round(ms_coo, 3),
+            "swtcf_coo_gedges_per_s": round(E / (ms_coo * 1e-3) / 1e9, 3),
+            "swtcf_convert_csr_ms": round(ms, 3),
             "swtcf_gedges_per_s": round(E / (ms * 1e-3) / 1e9, 3),
             "bcsr_tiles_ms": round(mt, 3), "bcsr_gedges_per_s": round(E / (mt * 1e-3) / 1e9, 3),
-            "timing": "SWTCF: CUDA events around the call, median of %d; BCSR: host wall clock "
-                      "of prepare (synchronises for the tile count) + fill, median of %d" % (reps, reps)}
+            "timing": "SWTCF: CUDA events around the call (COO: the reference's input form, "
+                      "dst-ascending; CSR: rows in order, so only the window digits are sorted), "
+                      "median of %d; BCSR: host wall clock of prepare (synchronises for the tile "
+                      "count) + fill, median of %d" % (reps, reps)}
 
 
 def config3(device, reps=10, warmup=3):
