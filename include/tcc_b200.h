@@ -250,6 +250,19 @@ tcc_status tcc_gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, cons
                            uint64_t n, float* out, uint64_t ldo, uint32_t F, uint32_t* bad_flag,
                            cudaStream_t stream);
 
+/* The hidden-layer epilogue of the GCN (train/tcgnn_conv_release.py:229-240:
+ * relu, then F.dropout with probability p, as separate torch ops there), fused
+ * into one pass: out[i] = in[i] > 0 && kept(seed, i) ? in[i] / (1 - p) : 0.
+ * kept(seed, i) is a counter-based draw (SplitMix64 finaliser of
+ * seed + (i + 1) * 0x9E3779B97F4A7C15; kept when its top 32 bits are >=
+ * ceil(p * 2^32)), so no mask is stored: the backward reads the forward's
+ * output, grad_in[i] = out[i] > 0 ? grad_out[i] / (1 - p) : 0.  n a multiple
+ * of 4, buffers 16-byte aligned, 0 <= p < 1; in == out is allowed. */
+tcc_status tcc_relu_dropout_forward(const float* in, float* out, uint64_t n, float p,
+                                    uint64_t seed, cudaStream_t stream);
+tcc_status tcc_relu_dropout_backward(const float* grad_out, const float* out, float* grad_in,
+                                     uint64_t n, float p, cudaStream_t stream);
+
 /* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
  * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):
  * C[num_rows x F] = diag(rs) * A * diag(cs) * B[num_cols x F]; row windows own
@@ -267,7 +280,8 @@ tcc_status tcc_bcsr_spmm(const tcc_bcsr* a, const float* B, uint64_t ldb, float*
  * this library (TCC_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads
  * the library until exit) instead of caller scratch; nothing is allocated.
  *  - Tilings whose plan exceeds TCC_NOALLOC_SCRATCH_BYTES are rejected with
- *    TCC_ERR_CAPACITY (about 24 bytes per window plus 1 per tile).
+ *    TCC_ERR_CAPACITY (about 24 bytes per window plus 2 per tile plus 1.1 MB,
+ *    tcc_pull_scratch_bytes: e.g. 300 K windows and 3.8 M tiles fit).
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress); make that first call before any stream capture.
  *  - Every call rebuilds the plan in the same array: calls that overlap on the

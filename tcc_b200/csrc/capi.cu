@@ -505,6 +505,22 @@ tcc_status tcc_gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, cons
     });
 }
 
+tcc_status tcc_relu_dropout_forward(const float* in, float* out, uint64_t n, float p,
+                                    uint64_t seed, cudaStream_t stream) {
+    return guarded("tcc_relu_dropout_forward", [&] {
+        TCC_REQUIRE(n == 0 || (in && out), "null argument");
+        tcc::relu_dropout_forward(in, out, n, p, seed, stream);
+    });
+}
+
+tcc_status tcc_relu_dropout_backward(const float* grad_out, const float* out, float* grad_in,
+                                     uint64_t n, float p, cudaStream_t stream) {
+    return guarded("tcc_relu_dropout_backward", [&] {
+        TCC_REQUIRE(n == 0 || (grad_out && out && grad_in), "null argument");
+        tcc::relu_dropout_backward(grad_out, out, grad_in, n, p, stream);
+    });
+}
+
 tcc_status tcc_pull_device_error(void* scratch, int* code, cudaStream_t stream) {
     return guarded("tcc_pull_device_error", [&] {
         TCC_REQUIRE(scratch && code, "scratch and code must not be NULL");

@@ -161,6 +161,29 @@ __device__ __forceinline__ void gather4(uint32_t dst, const CUtensorMap* tm, int
         : "memory");
 }
 
+// gather4 with an L2 eviction-priority policy (createpolicy) for the rows.
+__device__ __forceinline__ void gather4_hint(uint32_t dst, const CUtensorMap* tm, int32_t c0,
+                                             uint4 r, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(r.x), "r"(r.y), "r"(r.z),
+        "r"(r.w), "r"(bar), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // One contiguous global -> shared copy by the TMA unit, completing on `bar`
 // (16-byte aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes,
@@ -253,7 +276,7 @@ template <int NP, bool FULL, bool G4>
 __global__ void __launch_bounds__(kTW * 32, 1)
     pull_tma_kernel(const __grid_constant__ CUtensorMap tm, PullTiles a, Dense d, uint32_t bw,
                     uint32_t thr, int accumulate, uint32_t* __restrict__ err,
-                    unsigned long long wait_ns) {
+                    unsigned long long wait_ns, int l2hint) {
     extern __shared__ unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -289,6 +312,9 @@ __global__ void __launch_bounds__(kTW * 32, 1)
 
     // ---- metadata pipeline: B0 current (complete), B1 (cs in flight), B2 (idx in flight)
     const int grp = lane >> 3, krow = lane & 7;
+    // G4 with hints: bit 31 of a real gather index marks a hot row (real
+    // indices are below 2^31; padding 0xFFFFFFFF stays past num_in either way)
+    const bool hints = G4 && l2hint && a.hot != nullptr;
     auto load_idx = [&](uint32_t base, Batch& b) {
         const uint32_t t = base + grp;
         b.idx = kInvalid;
@@ -296,15 +322,18 @@ __global__ void __launch_bounds__(kTW * 32, 1)
         if (t < T1) {
             b.idx = ld_nc_u32(a.idx + (uint64_t)t * 8 + krow);
             b.bits = ld_nc_u64(a.bits + t);
+            if (hints && b.idx < a.num_in && ((__ldg(a.hot + t) >> krow) & 1u)) b.idx |= 0x80000000u;
         }
     };
+    auto real = [&](uint32_t v) { return hints ? (v & 0x7FFFFFFFu) : v; };
     auto load_cs = [&](Batch& b) {
-        b.cs = b.idx < a.num_in ? (d.cs ? __ldg(d.cs + b.idx) : 1.f) : 0.f;
+        const uint32_t r = real(b.idx);
+        b.cs = r < a.num_in ? (d.cs ? __ldg(d.cs + r) : 1.f) : 0.f;
     };
     auto finish = [&](Batch& b) {
         unsigned long long bits = b.bits;
         if (a.bits_transposed) bits = transpose8x8(bits);
-        const unsigned vm = __ballot_sync(0xffffffffu, b.idx < a.num_in);
+        const unsigned vm = __ballot_sync(0xffffffffu, real(b.idx) < a.num_in);
         const uint32_t valid = (vm >> (8 * grp)) & 0xFFu;
         b.bits = bits & (0x0101010101010101ull * (unsigned long long)valid);
     };
@@ -313,7 +342,8 @@ __global__ void __launch_bounds__(kTW * 32, 1)
     // G4: row coordinates of rows (lane & ~3) .. +3 of B0 (a padding column:
     // past the last row of X, read as zeros)
     auto make_quad = [&]() {
-        const uint32_t v = B0.idx < a.num_in ? B0.idx : a.num_in;
+        // the hot bit rides along in bit 31 (when hints are on)
+        const uint32_t v = real(B0.idx) < a.num_in ? B0.idx : a.num_in;
         const int q0 = lane & ~3;
         return make_uint4(__shfl_sync(0xffffffffu, v, q0), __shfl_sync(0xffffffffu, v, q0 + 1),
                           __shfl_sync(0xffffffffu, v, q0 + 2), __shfl_sync(0xffffffffu, v, q0 + 3));
@@ -348,9 +378,18 @@ __global__ void __launch_bounds__(kTW * 32, 1)
                 // rows krow .. krow + 3 of the tile, a padding column past the
                 // last row of X (zero fill); lanes krow = 0, 4 issue
                 if (krow == 0) mbar_arrive_tx(bar, 8 * pitch);
-                if ((krow & 3) == 0)
-                    gather4(smem_u32(sdata + q * kStageBytes) + (krow >> 2) * half, &tm, fb, quad,
-                            bar);
+                if ((krow & 3) == 0) {
+                    const uint32_t dst = smem_u32(sdata + q * kStageBytes) + (krow >> 2) * half;
+                    if (hints) {
+                        const bool hot = ((quad.x | quad.y | quad.z | quad.w) >> 31) != 0;
+                        const uint4 rc = make_uint4(quad.x & 0x7FFFFFFFu, quad.y & 0x7FFFFFFFu,
+                                                    quad.z & 0x7FFFFFFFu, quad.w & 0x7FFFFFFFu);
+                        gather4_hint(dst, &tm, fb, rc, bar,
+                                     hot ? policy_evict_last() : policy_evict_first());
+                    } else {
+                        gather4(dst, &tm, fb, quad, bar);
+                    }
+                }
             } else {
                 if (krow == 0) mbar_arrive_tx(bar, 8 * rowbytes);
                 const float* row =
@@ -597,8 +636,9 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
              : bw < 64  ? pick(Fa{}, One{})
                         : pick(Fa{}, Two{});
     TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    const int l2hint = l2_hints_requested() ? 1 : 0;
     k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(tm, a, d, bw, thr, accumulate, err,
-                                                       (unsigned long long)wait_limit_ns());
+                                                       (unsigned long long)wait_limit_ns(), l2hint);
     TCC_CUDA(cudaGetLastError());
 }
 

@@ -22,6 +22,8 @@
 #include "tile_mma.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <atomic>
 #include <cstddef>
 #include <mutex>
@@ -66,8 +68,16 @@ struct PlanHeader {
     uint32_t pad[14];
 };
 
+// Hot-row selection: use counts of the gathered rows in a direct-mapped
+// table of kSketch counters (row r counts at r mod kSketch: exact for up to
+// kSketch rows, an overestimate beyond), then the most used rows up to
+// kHotRows (one 128-float slice each: ~80 MB of L2) are "hot".
+constexpr uint32_t kSketch = 1u << 18;
+constexpr uint32_t kCountBins = 1u << 14;
+constexpr uint32_t kHotRows = 160u << 10;
+
 struct PlanLayout {
-    size_t cstart, desc, heavy, tmp, total;
+    size_t cstart, desc, heavy, tmp, hot, sketch, hist, total;
     uint64_t max_chunks;
     PlanLayout(uint32_t W, uint32_t T) {
         auto al = [](size_t b) { return (b + 255) / 256 * 256; };
@@ -76,9 +86,62 @@ struct PlanLayout {
         desc = cstart + al(((size_t)W + 1) * 4);
         heavy = desc + al(max_chunks * 16);
         tmp = heavy + al(((size_t)W + 1) * 4);
-        total = tmp + al(scan_tmp_bytes((uint64_t)W + 1));
+        hot = tmp + al(scan_tmp_bytes((uint64_t)W + 1));
+        sketch = hot + al(std::max<size_t>(T, 1));
+        hist = sketch + al((size_t)kSketch * 4);
+        total = hist + al((size_t)kCountBins * 4 + 16);
     }
 };
+
+__global__ void hot_count_kernel(const uint32_t* __restrict__ idx, uint64_t n, uint32_t num_in,
+                                 uint32_t* __restrict__ sketch) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t r = idx[i];
+        if (r < num_in) atomicAdd(&sketch[r & (kSketch - 1)], 1u);
+    }
+}
+
+__global__ void hot_hist_kernel(const uint32_t* __restrict__ sketch, uint32_t* __restrict__ hist) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < kSketch; i += gridDim.x * blockDim.x) {
+        const uint32_t c = sketch[i];
+        if (c > 1) atomicAdd(&hist[min(c, kCountBins - 1)], 1u);
+    }
+}
+
+// One block: the smallest use count K (>= 2) whose rows with count >= K fit
+// kHotRows; stored at hist[kCountBins] (kCountBins = none hot).
+__global__ void hot_threshold_kernel(uint32_t* __restrict__ hist) {
+    __shared__ uint32_t done;
+    if (threadIdx.x == 0) {
+        uint64_t rows = 0;
+        uint32_t K = kCountBins;
+        for (uint32_t c = kCountBins - 1; c >= 2; --c) {
+            rows += hist[c];
+            if (rows > kHotRows) break;
+            K = c;
+        }
+        hist[kCountBins] = K;
+        done = 1;
+    }
+    __syncthreads();
+    (void)done;
+}
+
+__global__ void hot_mask_kernel(const uint32_t* __restrict__ idx, uint32_t T, uint32_t num_in,
+                                const uint32_t* __restrict__ sketch,
+                                const uint32_t* __restrict__ hist, uint8_t* __restrict__ hot) {
+    const uint32_t K = hist[kCountBins];
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+        uint32_t m = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t r = idx[(uint64_t)t * 8 + k];
+            if (r < num_in && sketch[r & (kSketch - 1)] >= K) m |= 1u << k;
+        }
+        hot[t] = (uint8_t)m;
+    }
+}
 
 __global__ void plan_count_kernel(const uint32_t* __restrict__ off, uint32_t W,
                                   uint32_t* __restrict__ nch) {
@@ -620,6 +683,13 @@ size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
     return PlanLayout(num_windows, num_tiles).total;
 }
 
+// TCC_PULL_L2=hot: the bulk-copy pull kernel gives hot rows an evict-last and
+// the others an evict-first L2 priority (the plan then builds the hot mask).
+bool l2_hints_requested() {
+    const char* e = std::getenv("TCC_PULL_L2");
+    return e && std::strcmp(e, "hot") == 0;
+}
+
 // Work plan of the register-gather kernel in the scratch: chunk descriptors,
 // split windows and a zeroed header (which also clears the error word).
 void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStream_t s) {
@@ -636,6 +706,22 @@ void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStre
     plan_count_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart);
     exclusive_scan<uint32_t>(cstart, cstart, W, cstart + W, base + L.tmp, s);
     plan_fill_kernel<<<ceil_div(W, 256), 256, 0, s>>>(a.win_offset, W, cstart, desc, heavy, hdr);
+    // hot gathered rows of the tiling (the column-window passes gather
+    // through super-window slots: no hot mask there)
+    if (!a.sw_rows && a.num_tiles > 0 && !l2_hints_requested()) {
+        TCC_CUDA(cudaMemsetAsync(base + L.hot, 0, a.num_tiles, s));  // defined: no hot rows
+    } else if (!a.sw_rows && a.num_tiles > 0) {
+        uint32_t* sketch = reinterpret_cast<uint32_t*>(base + L.sketch);
+        uint32_t* hist = reinterpret_cast<uint32_t*>(base + L.hist);
+        const unsigned g = (unsigned)std::max(1, sm_count() * 8);
+        TCC_CUDA(cudaMemsetAsync(sketch, 0, (size_t)kSketch * 4, s));
+        TCC_CUDA(cudaMemsetAsync(hist, 0, (size_t)kCountBins * 4 + 16, s));
+        hot_count_kernel<<<g, 256, 0, s>>>(a.idx, (uint64_t)a.num_tiles * 8, a.num_in, sketch);
+        hot_hist_kernel<<<g, 256, 0, s>>>(sketch, hist);
+        hot_threshold_kernel<<<1, 32, 0, s>>>(hist);
+        hot_mask_kernel<<<g, 256, 0, s>>>(a.idx, a.num_tiles, a.num_in, sketch, hist,
+                                          reinterpret_cast<uint8_t*>(base + L.hot));
+    }
     TCC_CUDA(cudaGetLastError());
 }
 
@@ -672,7 +758,12 @@ void pull_spmm(const PullTiles& a, const Dense& d, uint32_t tc_threshold, int ac
         return;
     }
     if (tma) {
-        pull_tma(a, d, tc_threshold, accumulate, &hdr->pad[0], s);
+        PullTiles at = a;
+        // the hot-row mask exists when the plan was built (plan_ready, or
+        // built above); the no-allocation entry builds none for this kernel
+        if (!a.sw_rows && a.num_tiles > 0 && (plan_ready || keep_plan))
+            at.hot = reinterpret_cast<const uint8_t*>(base + L.hot);
+        pull_tma(at, d, tc_threshold, accumulate, &hdr->pad[0], s);
         return;
     }
     if (!accumulate)

@@ -19,6 +19,11 @@ struct PullTiles {
     uint32_t S = 0;
     uint32_t num_out;   // output rows (guards the last window)
     uint32_t num_in;    // gather rows (indices >= num_in are padding)
+    // per tile, bit k: gathered row k is among the most used rows of the
+    // tiling (built with the work plan; NULL = unknown).  The bulk-copy pull
+    // kernel gives the copies of those rows an L2 evict-last priority and the
+    // others evict-first, so that the rows most tiles share stay in L2.
+    const uint8_t* hot = nullptr;
 };
 
 // Dense operands.  cs scales gathered rows, rs scales output rows (NULL = 1).
@@ -49,6 +54,8 @@ struct FeatureStore {
 };
 
 size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
+// TCC_PULL_L2=hot is set: hot-row L2 hints in the bulk-copy pull kernel.
+bool l2_hints_requested();
 // Builds the pull work plan in `scratch` on stream s (what plan_ready = 1 reuses).
 void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStream_t s);
 // keep_plan = false: the caller never passes plan_ready = 1 for this scratch
@@ -69,6 +76,12 @@ void pull_umma(const PullTiles& a, const Dense& d, int accumulate, uint32_t* err
 // rows.cu: out[i] = X[idx[i]] (halo pack of the row-partitioned SpMM).
 void gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, const int64_t* idx, uint64_t n,
                  float* out, uint64_t ldo, uint32_t F, uint32_t* bad, cudaStream_t s);
+// gcn_ops.cu: fused ReLU + dropout of a GCN hidden layer and its backward.
+uint32_t dropout_threshold(float p);
+void relu_dropout_forward(const float* in, float* out, uint64_t n, float p, uint64_t seed,
+                          cudaStream_t s);
+void relu_dropout_backward(const float* grad_out, const float* out, float* grad_in, uint64_t n,
+                           float p, cudaStream_t s);
 // Offset of the device error word inside a pull scratch.
 constexpr size_t kPullErrorOffset = 8;
 

@@ -114,6 +114,46 @@ class CNICSPMMFunction(torch.autograd.Function):
                 grad_X, grad_weights, None, None)
 
 
+# ----------------------------------------------------- ReLU + dropout --
+
+class ReluDropout(torch.autograd.Function):
+    """relu then dropout(p) in one pass (tcc_relu_dropout_forward); the
+    backward needs only the output (tcc_relu_dropout_backward).  The reference
+    runs torch.relu and F.dropout separately (train/tcgnn_conv_release.py:229-240)."""
+
+    @staticmethod
+    def forward(ctx, x, p: float, seed: int):
+        import ctypes as C
+        from . import _lib as L
+        x = x.contiguous()
+        out = torch.empty_like(x)
+        L.call("tcc_relu_dropout_forward", C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()),
+               x.numel(), float(p), int(seed) & ((1 << 64) - 1),
+               C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        ctx.p = float(p)
+        ctx.save_for_backward(out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        import ctypes as C
+        from . import _lib as L
+        (out,) = ctx.saved_tensors
+        grad_out = grad_out.contiguous()
+        grad_in = torch.empty_like(out)
+        L.call("tcc_relu_dropout_backward", C.c_void_p(grad_out.data_ptr()),
+               C.c_void_p(out.data_ptr()), C.c_void_p(grad_in.data_ptr()), out.numel(), ctx.p,
+               C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return grad_in, None, None
+
+
+def relu_dropout(x: torch.Tensor, p: float, seed: int, training: bool = True) -> torch.Tensor:
+    """dropout(relu(x), p) fused; plain relu when not training or p == 0."""
+    if not training or p == 0.0:
+        return torch.relu(x)
+    return ReluDropout.apply(x, p, seed)
+
+
 # ------------------------------------------------------------- TiledGraph --
 
 class TiledGraph:
@@ -192,13 +232,17 @@ class GCNConv(torch.nn.Module):
 class GCN(torch.nn.Module):
     """Two-layer GCN of train/tcgnn_conv_release.py:196-268."""
 
-    def __init__(self, num_features, hidden_dim, num_classes, dropout=0.5):
+    def __init__(self, num_features, hidden_dim, num_classes, dropout=0.5, seed=0):
         super().__init__()
         self.conv1 = GCNConv(num_features, hidden_dim, first_layer=True)
         self.conv_final = GCNConv(hidden_dim, num_classes)
-        self.dropout = torch.nn.Dropout(p=dropout)
+        self.p = dropout
+        self._seed = seed
+        self._calls = 0
 
     def forward(self, graph: TiledGraph, x):
-        h = torch.relu(self.conv1(graph, x))
-        h = self.dropout(h)
+        # relu + dropout in one pass; a fresh dropout draw per call
+        self._calls += 1
+        h = relu_dropout(self.conv1(graph, x), self.p, self._seed * 1_000_003 + self._calls,
+                         self.training)
         return self.conv_final(graph, h)

@@ -51,6 +51,7 @@ import torch.distributed as dist
 from . import graphs as G
 from . import tiles as T
 from .feature_store import FeatureStore
+from .gcn import relu_dropout
 from .partition import DistGraph, balanced_bounds, nccl_options
 
 
@@ -165,8 +166,8 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
         used = torch.cuda.Event()
         store.stage_cold(side)
         ready.record(side)
-    drop = torch.Generator(device=device)
-    drop.manual_seed(cfg["seed"] * 1000 + rank)
+    drop_seed = (cfg["seed"] * 1000 + rank) << 20  # dropout draw of epoch e: drop_seed + e
+    epoch_no = [start_epoch]
     cls_pad = (cfg["classes"] + 3) // 4 * 4  # transform-first SpMM width, multiple of 4
 
     def epoch(stage_next: bool):
@@ -182,9 +183,9 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
                 ready.record(side)
         else:
             Z1 = _store_aggregate(R["tiles_g"], store, R["rs"])
-        H1 = torch.relu(Z1 @ W1)
-        keep = torch.rand(H1.shape, generator=drop, device=device) >= cfg["dropout"]
-        H1 = H1 * keep / (1.0 - cfg["dropout"])
+        # relu + dropout fused (one pass; the backward reads only H1)
+        H1 = relu_dropout(Z1 @ W1, cfg["dropout"], drop_seed + epoch_no[0])
+        epoch_no[0] += 1
         if transform_first:
             P = torch.nn.functional.pad(H1 @ W2, (0, cls_pad - cfg["classes"]))
             logits = _DistAggregate.apply(R["dg"], P)[:, :cfg["classes"]]

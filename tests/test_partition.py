@@ -92,3 +92,25 @@ def test_balanced_bounds():
     b = balanced_bounds(deg, 2)
     assert b[0] == 0 and b[-1] == 10 and 0 < b[1] < 10
     assert balanced_bounds(deg, 1) == [0, 10]
+
+
+def test_tile_balanced_bounds():
+    """Row bounds on window boundaries with about equal tiles + per-window work."""
+    import torch
+    from tcc_b200.partition import tile_balanced_bounds
+    gen = torch.Generator().manual_seed(0)
+    n = 8 * 1000 + 5
+    W = (n + 7) // 8
+    per = torch.randint(0, 40, (W,), generator=gen)
+    per[:10] = 5000  # hub windows at the front
+    off = torch.zeros(W + 1, dtype=torch.int64)
+    off[1:] = torch.cumsum(per, 0)
+    for parts in (2, 3, 8):
+        b = tile_balanced_bounds(off, n, parts)
+        assert b[0] == 0 and b[-1] == n and len(b) == parts + 1
+        assert all(x < y for x, y in zip(b, b[1:]))
+        assert all(x % 8 == 0 for x in b[1:-1])
+        cost = [float(per[b[k] // 8:(b[k + 1] + 7) // 8].sum()) + 2.0 * ((b[k + 1] - b[k] + 7) // 8)
+                for k in range(parts)]
+        # every part within one heavy window of the ideal share
+        assert max(cost) <= sum(cost) / parts + 5000 + 50
