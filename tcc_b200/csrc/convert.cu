@@ -46,28 +46,54 @@ __global__ void keys_from_coo_kernel(const uint32_t* __restrict__ dst,
 }
 
 // CSR -> keys.  mode 0: window = row (BCSR); mode 1: window = col (BCSC, SWTCF).
-// One warp per row, its lanes striding over the row's nonzeros (coalesced).
-__global__ void keys_from_csr_kernel(const uint64_t* __restrict__ rowptr,
-                                     const uint32_t* __restrict__ col, uint32_t rows,
-                                     uint32_t cols, uint64_t n, int mode, int ybits,
-                                     uint64_t* __restrict__ keys, uint32_t* __restrict__ vals,
-                                     uint32_t* err) {
-    const int lane = threadIdx.x & 31;
-    const uint64_t warps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
-    for (uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-        // the last row also takes any entries past rowptr[rows] (as before)
-        const uint64_t b = rowptr[r], e = r + 1 == rows ? n : min(rowptr[r + 1], n);
-        for (uint64_t i = b + lane; i < e; i += 32) {
-            uint32_t c = col[i];
-            if (c >= cols) {
-                raise_error(err, TCC_DEVERR_INDEX_RANGE);
-                c = 0;
-            }
-            const uint32_t x = mode == 0 ? (uint32_t)r : c;
-            const uint32_t y = mode == 0 ? c : (uint32_t)r;
-            keys[i] = ((uint64_t)(x >> 3) << ybits) | y;
-            vals[i] = x & 7u;
+// A block owns kKeyTile consecutive nonzeros; its first thread finds the rows
+// of the first and last one (binary searches over rowptr), the block stages
+// rowptr over that row range in shared memory when it fits, and every thread
+// finds its nonzero's row by a binary search over that short range (the
+// whole-array search per nonzero, and a warp per row, which serialises on
+// the hub rows of power-law graphs, were both slower).
+constexpr int kKeyTile = 2048;
+constexpr int kKeyRows = 2048;
+__device__ __forceinline__ uint32_t row_of(const uint64_t* rp, uint32_t lo, uint32_t hi, uint64_t i) {
+    // largest r in [lo, hi] with rp[r] <= i
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo + 1) / 2;
+        if (rp[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(256) keys_from_csr_kernel(
+    const uint64_t* __restrict__ rowptr, const uint32_t* __restrict__ col, uint32_t rows,
+    uint32_t cols, uint64_t n, int mode, int ybits, uint64_t* __restrict__ keys,
+    uint32_t* __restrict__ vals, uint32_t* err) {
+    __shared__ uint64_t srp[kKeyRows + 1];
+    __shared__ uint32_t range[2];
+    const uint64_t b0 = (uint64_t)blockIdx.x * kKeyTile;
+    if (b0 >= n || rows == 0) return;
+    const uint64_t b1 = min(n, b0 + kKeyTile);
+    if (threadIdx.x == 0) {
+        const uint32_t last = rows - 1;
+        range[0] = row_of(rowptr, 0, last, b0);
+        range[1] = row_of(rowptr, range[0], last, b1 - 1);
+    }
+    __syncthreads();
+    const uint32_t r0 = range[0], r1 = range[1];
+    const bool staged = r1 - r0 < (uint32_t)kKeyRows;
+    if (staged)
+        for (uint32_t j = threadIdx.x; j <= r1 - r0; j += blockDim.x) srp[j] = rowptr[r0 + j];
+    __syncthreads();
+    for (uint64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) {
+        const uint32_t r = staged ? r0 + row_of(srp, 0, r1 - r0, i) : row_of(rowptr, r0, r1, i);
+        uint32_t c = col[i];
+        if (c >= cols) {
+            raise_error(err, TCC_DEVERR_INDEX_RANGE);
+            c = 0;
         }
+        const uint32_t x = mode == 0 ? r : c;
+        const uint32_t y = mode == 0 ? c : r;
+        keys[i] = ((uint64_t)(x >> 3) << ybits) | y;
+        vals[i] = x & 7u;
     }
 }
 
@@ -408,11 +434,8 @@ __global__ void __launch_bounds__(kThreads) repeat_cache_kernel(
 }
 
 inline unsigned blocks(uint64_t n) { return (unsigned)((n + kThreads - 1) / kThreads); }
-// keys_from_csr_kernel: a warp per row, grid-stride over rows
-inline unsigned csr_blocks(uint64_t rows) {
-    const uint64_t want = (rows + kThreads / 32 - 1) / (kThreads / 32);
-    return (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(want, (uint64_t)sm_count() * 64));
-}
+// keys_from_csr_kernel: one block per kKeyTile nonzeros
+inline unsigned csr_blocks(uint64_t nnz) { return (unsigned)std::max<uint64_t>(1, (nnz + kKeyTile - 1) / kKeyTile); }
 
 }  // namespace
 
@@ -529,11 +552,12 @@ void swtcf_convert(const uint32_t* d_dst, const uint32_t* d_src, const uint64_t*
     const int swbits = std::max(1, bits_for(SW));
     GroupBuffers b = ws.g;
     TCC_CUDA(cudaMemsetAsync(ws.small, 0, 64, s));
+    TCC_REQUIRE(d_dst || m->rows > 0, "CSR conversion of a matrix without rows");
     if (d_dst) {
         keys_from_coo_kernel<<<blocks(nnz), kThreads, 0, s>>>(d_dst, d_src, nnz, m->rows, m->cols,
                                                              ybits, b.keys, b.vals, ws.small);
     } else {
-        keys_from_csr_kernel<<<csr_blocks(m->rows), kThreads, 0, s>>>(
+        keys_from_csr_kernel<<<csr_blocks(nnz), kThreads, 0, s>>>(
             d_rowptr, d_col, m->rows, m->cols, nnz, 1, ybits, b.keys, b.vals, ws.small);
     }
     build_windows(b, nnz, wbits + ybits, ybits, W, ws.wcnt, ws.wgstart, ws.tiles,
@@ -625,7 +649,7 @@ uint64_t tiles_prepare(TilesWorkspace& ws, int kind, const uint64_t* d_rowptr,
     const int wbits = std::max(1, bits_for(ws.W));
     TCC_CUDA(cudaMemsetAsync(ws.small, 0, 64, s));
     if (nnz)
-        keys_from_csr_kernel<<<csr_blocks(rows), kThreads, 0, s>>>(
+        keys_from_csr_kernel<<<csr_blocks(nnz), kThreads, 0, s>>>(
             d_rowptr, d_col, rows, cols, nnz, kind == TCC_TILES_BCSR ? 0 : 1, ws.ybits, ws.g.keys,
             ws.g.vals, ws.small);
     build_windows(ws.g, nnz, wbits + ws.ybits, ws.ybits, ws.W, ws.wcnt, ws.wgstart, ws.tiles,
