@@ -263,6 +263,17 @@ tcc_status tcc_relu_dropout_forward(const float* in, float* out, uint64_t n, flo
 tcc_status tcc_relu_dropout_backward(const float* grad_out, const float* out, float* grad_in,
                                      uint64_t n, float p, cudaStream_t stream);
 
+/* No counterpart in the reference.  The other half of the row-partitioned
+ * transposed SpMM's exchange: a rank computes partial rows of A^T.G for the
+ * remote columns its rows reference and returns them to their owners, who add
+ * them in: out[idx[i], :F] += in[i, :F] for i < n (idx may repeat; vector fp32
+ * reductions, so the order of additions is not fixed).  An index outside
+ * [0, num_rows) is skipped and sets the device word *bad_flag (may be NULL).
+ * F and the strides multiples of 4, in and out 16-byte aligned. */
+tcc_status tcc_scatter_add_rows(const float* in, uint64_t ldi, const int64_t* idx, uint64_t n,
+                                float* out, uint64_t ldo, uint64_t num_rows, uint32_t F,
+                                uint32_t* bad_flag, cudaStream_t stream);
+
 /* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
  * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):
  * C[num_rows x F] = diag(rs) * A * diag(cs) * B[num_cols x F]; row windows own

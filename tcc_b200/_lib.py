@@ -106,6 +106,7 @@ PROTOTYPES = {
     "tcc_bcsr_spmm_noalloc": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp,
                                     _i, _vp]),
     "tcc_noalloc_device_error": (_st, [C.POINTER(_i), _vp]),
+    "tcc_scatter_add_rows": (_st, [_vp, _u64, _vp, _u64, _vp, _u64, _u64, _u32, _vp, _vp]),
     "tcc_relu_dropout_forward": (_st, [_vp, _vp, _u64, C.c_float, _u64, _vp]),
     "tcc_relu_dropout_backward": (_st, [_vp, _vp, _vp, _u64, C.c_float, _vp]),
     "tcc_bcsr_spmm_t": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),

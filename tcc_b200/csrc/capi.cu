@@ -505,6 +505,15 @@ tcc_status tcc_gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, cons
     });
 }
 
+tcc_status tcc_scatter_add_rows(const float* in, uint64_t ldi, const int64_t* idx, uint64_t n,
+                                float* out, uint64_t ldo, uint64_t num_rows, uint32_t F,
+                                uint32_t* bad_flag, cudaStream_t stream) {
+    return guarded("tcc_scatter_add_rows", [&] {
+        TCC_REQUIRE(n == 0 || (in && idx && out), "in, idx and out must not be NULL");
+        tcc::scatter_add_rows(in, ldi, idx, n, out, ldo, num_rows, F, bad_flag, stream);
+    });
+}
+
 tcc_status tcc_relu_dropout_forward(const float* in, float* out, uint64_t n, float p,
                                     uint64_t seed, cudaStream_t stream) {
     return guarded("tcc_relu_dropout_forward", [&] {

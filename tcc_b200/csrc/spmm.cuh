@@ -73,6 +73,9 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
 // TF32 tensor cores), F a multiple of 128, dense X.
 bool pull_umma_eligible(const PullTiles& a, const Dense& d, uint32_t tc_threshold);
 void pull_umma(const PullTiles& a, const Dense& d, int accumulate, uint32_t* err, cudaStream_t s);
+// rows.cu: out[idx[i]] += in[i] (the transposed pass's returned halo rows).
+void scatter_add_rows(const float* in, uint64_t ldi, const int64_t* idx, uint64_t n, float* out,
+                      uint64_t ldo, uint64_t num_rows, uint32_t F, uint32_t* bad, cudaStream_t s);
 // rows.cu: out[i] = X[idx[i]] (halo pack of the row-partitioned SpMM).
 void gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, const int64_t* idx, uint64_t n,
                  float* out, uint64_t ldo, uint32_t F, uint32_t* bad, cudaStream_t s);

@@ -84,7 +84,8 @@ class DistGraph:
     """
 
     def __init__(self, rowptr: torch.Tensor, col: torch.Tensor, bounds: list, group=None,
-                 rs_local=None, cs_global=None, tc_threshold: int = 12, build_tiles: bool = True):
+                 rs_local=None, cs_global=None, tc_threshold: int = 12, build_tiles: bool = True,
+                 symmetric: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -135,7 +136,9 @@ class DistGraph:
         self._side = None
         self._tstream = None
         self.comm_sms = 32  # SMs left to the exchange during the local tiles (measured best of 0-32)
+        self.symmetric = symmetric
         self.tiles_loc = self.tiles_halo = None
+        self.tiles_loc_t = self.tiles_halo_t = None  # BCSC tilings, built by the first spmm_t
         if build_tiles:
             from . import tiles
             self.tiles_loc = tiles.from_csr(self.loc_rowptr, self.loc_col, self.n_local,
@@ -267,9 +270,53 @@ class DistGraph:
             timer["done1"] = _event(main)
         return Y, Z
 
-    # For a symmetric A (the GCN-normalised graphs) Aᵀ·G on the same partition
-    # is A·G.
-    spmm_t = spmm
+    def spmm_t(self, G_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Z[P_g] = (diag(cs) Aᵀ diag(rs) G)[P_g] with G and Z split like the rows.
+
+        symmetric=True: Aᵀ = A, so this is the forward pass on the same
+        partition.  Otherwise the exchange runs backwards: the rank's rows give
+        partial sums for the local columns (kept) and for its halo columns,
+        whose rows go back to their owners -- the all-to-all of the forward
+        pass with the send and receive counts swapped -- and each owner adds
+        the rows it receives into its own (tcc_scatter_add_rows; the rows it
+        receives are the ones it sent in the forward exchange).  The local
+        columns' pull overlaps the returning exchange."""
+        if self.symmetric:
+            return self.spmm(G_local, out)
+        import ctypes as C
+        from . import tiles
+        from . import _lib as L
+        G_local = G_local.contiguous()
+        if self.tiles_loc_t is None:
+            self.tiles_loc_t = tiles.from_csr(self.loc_rowptr, self.loc_col, self.n_local,
+                                              self.n_local, kind="bcsc")
+            if self.halo.numel():
+                self.tiles_halo_t = tiles.from_csr(self.halo_rowptr, self.halo_col, self.n_local,
+                                                   int(self.halo.numel()), kind="bcsc")
+        main = torch.cuda.current_stream(G_local.device)
+        work = None
+        if self.tiles_halo_t is not None:
+            # partial rows for the halo columns, scaled by their column scale
+            Zh = self._buf("halo_part", self.halo_rows, G_local)
+            tiles.bcsc_spmm_t(self.tiles_halo_t, G_local, Zh, tc_threshold=self.tc_threshold,
+                              rs=self.rs, cs=self.cs_halo)
+            back = self._buf("returned", int(self.send_idx.numel()), G_local)
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=G_local.device, priority=-1)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                work = dist.all_to_all_single(back, Zh, self.send_counts, self.recv_counts,
+                                              group=self.group, async_op=True)
+        Z = tiles.bcsc_spmm_t(self.tiles_loc_t, G_local, out, tc_threshold=self.tc_threshold,
+                              rs=self.rs, cs=self.cs_local)
+        if work is not None:
+            work.wait()
+            if self.send_idx.numel():
+                L.call("tcc_scatter_add_rows", C.c_void_p(back.data_ptr()), back.stride(0),
+                       C.c_void_p(self.send_idx.data_ptr()), self.send_idx.numel(),
+                       C.c_void_p(Z.data_ptr()), Z.stride(0), Z.shape[0], Z.shape[1], None,
+                       C.c_void_p(main.cuda_stream))
+        return Z
 
 
 def tile_balanced_bounds(window_offset: torch.Tensor, num_rows: int, parts: int,

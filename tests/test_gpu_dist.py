@@ -1,5 +1,7 @@
 """Row-partitioned SpMM over NCCL: every rank's rows equal the single-GPU
-result.  Spawns one process per visible GPU (2 or more); skipped otherwise."""
+result -- the forward pass, the pipelined pair the bench times, and the
+transposed pass of a directed graph (partial rows returned to their owners).
+Spawns one process per visible GPU (2 or more); skipped otherwise."""
 import os
 import socket
 
@@ -51,6 +53,28 @@ def _worker(rank, world, port, q):
         full = tiles.from_csr(rowptr, col, deg.numel(), deg.numel(), kind="bcsr")
         Yref = tiles.bcsr_spmm(full, X, tc_threshold=65, rs=s, cs=s)[r0:r1]
         err = (torch.linalg.norm(Y - Yref) / torch.linalg.norm(Yref)).item()
+        # the pipelined pair of the bench's step (A symmetric: Z = A[P_g, :] G)
+        Gm = torch.randn((deg.numel(), 64), generator=gen, device=dev)
+        Y2, Z2 = torch.empty_like(Y), torch.empty_like(Y)
+        dg.spmm_pair(X[r0:r1].contiguous(), Y2, Gm[r0:r1].contiguous(), Z2)
+        Zref = tiles.bcsr_spmm(full, Gm, tc_threshold=65, rs=s, cs=s)[r0:r1]
+        err = max(err, (torch.linalg.norm(Y2 - Yref) / torch.linalg.norm(Yref)).item(),
+                  (torch.linalg.norm(Z2 - Zref) / torch.linalg.norm(Zref)).item())
+        # a directed graph: the transposed pass returns partial rows to owners
+        drp, dcol, _ = G.rmat_gpu(15, 16 << 15, seed=10, device=dev, symmetric=False,
+                                  loops=False)
+        ddeg = torch.diff(drp)
+        rsd = torch.where(ddeg > 0, 1.0 / ddeg.clamp(min=1).to(torch.float32),
+                          torch.zeros_like(ddeg, dtype=torch.float32))
+        db = balanced_bounds(ddeg, world)
+        a0, a1 = db[rank], db[rank + 1]
+        ddg = DistGraph((drp[a0:a1 + 1] - drp[a0]).contiguous(),
+                        dcol[drp[a0]:drp[a1]].contiguous(), db, rs_local=rsd[a0:a1].contiguous(),
+                        cs_global=None, tc_threshold=65)
+        Zd = ddg.spmm_t(Gm[a0:a1].contiguous())
+        dfull = tiles.from_csr(drp, dcol, ddeg.numel(), ddeg.numel(), kind="bcsc")
+        Zdref = tiles.bcsc_spmm_t(dfull, Gm, tc_threshold=65, rs=rsd)[a0:a1]
+        err = max(err, (torch.linalg.norm(Zd - Zdref) / torch.linalg.norm(Zdref)).item())
         torch.cuda.synchronize()
         q.put((rank, err, dg.halo_rows))
     finally:
