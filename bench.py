@@ -991,11 +991,13 @@ def run_reference(args, rank, world, local_rank):
     sh = s.cpu().numpy()
     X = features(n, 1000, dev)
     Xh = X.cpu().numpy()
+    # each step a bounded sample (~2 s of CPU work), so the whole run stays
+    # within a few minutes at the driver's --steps / --warmup
     for _ in range(args.warmup):
-        cpu_baseline(g, Xh, sh, sh, budget_s=2.0)
+        cpu_baseline(g, Xh, sh, sh, budget_s=1.0)
     vals = []
     for _ in range(args.steps):
-        cb = cpu_baseline(g, Xh, sh, sh, budget_s=4.0)
+        cb = cpu_baseline(g, Xh, sh, sh, budget_s=2.0)
         vals.append(cb["value"])
     cb["value"] = statistics.median(vals)
     ts = torch_sparse_baseline(rowptr, col, s, X, budget_s=4.0)
