@@ -2,8 +2,9 @@
 
 Pins: the reference's closed-form known-answer SpMM test
 (src/swtcf_spmm_main.cu:33-112) and its layout validators
-(src/swtcf_convert_main.cu:36-310), both restated in oracle/tcc_oracle.c, plus
-the golden fixtures generated from the reference build (tests/golden/).
+(src/swtcf_convert_main.cu:36-310), both restated in oracle/tcc_oracle.c.  The
+golden vectors produced by the reference build itself (tests/golden/) are
+checked in tests/test_golden.py.
 """
 import numpy as np
 import pytest
