@@ -399,7 +399,13 @@ __global__ void __launch_bounds__(kThreads) repeat_cache_kernel(
         const uint32_t r = c + tid;
         uint32_t o = r < re ? occ[r] : 0;
         if (o > TCC_SWTCF_MAX_SUPER_WINDOW) o = 0;
-        const bool live = o >= 2 && base[o] < 32;
+        // a row can still be cached while its occurrence bucket has ranks
+        // below 32 left (run[] counts the bucket's rows in earlier chunks)
+        const bool live = o >= 2 && base[o] + run[o] < 32;
+        if (!__syncthreads_or(live)) {  // nothing left to rank in this chunk
+            if (r < re) row_cache_slot[r] = 0xFF;
+            continue;
+        }
         const uint32_t key = live ? o : 0;
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         const uint32_t lr = __popc(peers & lanemask_lt());

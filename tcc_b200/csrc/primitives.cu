@@ -135,6 +135,7 @@ struct SortSmem {
     uint32_t vals[kSortTile];
     uint32_t warp_cnt[kSortWarps][kRadix + 1];  // digit counts, then prefixes; [kRadix]: sentinel
     uint32_t digit_start[kRadix];
+    uint32_t out_base[kRadix];  // global position of the tile's first key of each digit
     uint32_t scan_ws[kScanThreads / 32 + 1];
 };
 
@@ -196,6 +197,8 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
     uint32_t total;
     const uint32_t start = block_exclusive<uint32_t>(run, S.scan_ws, total);
     S.digit_start[tid] = start;
+    // one global offset per digit, read once here instead of once per key below
+    S.out_base[tid] = offsets[(uint64_t)tid * num_tiles + blockIdx.x] - start;
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
@@ -212,8 +215,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
         if (p < tile_n) {
             const uint64_t key = S.keys[p];
             const uint32_t dg = (uint32_t)(key >> shift) & 0xFFu;
-            const uint64_t g = (uint64_t)offsets[(uint64_t)dg * num_tiles + blockIdx.x] +
-                               (p - S.digit_start[dg]);
+            const uint64_t g = (uint64_t)S.out_base[dg] + p;
             keys_out[g] = key;
             vals_out[g] = S.vals[p];
         }

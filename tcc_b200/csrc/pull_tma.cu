@@ -384,8 +384,12 @@ __global__ void __launch_bounds__(kTW * 32, 1)
                         const bool hot = ((quad.x | quad.y | quad.z | quad.w) >> 31) != 0;
                         const uint4 rc = make_uint4(quad.x & 0x7FFFFFFFu, quad.y & 0x7FFFFFFFu,
                                                     quad.z & 0x7FFFFFFFu, quad.w & 0x7FFFFFFFu);
-                        gather4_hint(dst, &tm, fb, rc, bar,
-                                     hot ? policy_evict_last() : policy_evict_first());
+                        if (hot)
+                            gather4_hint(dst, &tm, fb, rc, bar, policy_evict_last());
+                        else if (l2hint == 1)
+                            gather4_hint(dst, &tm, fb, rc, bar, policy_evict_first());
+                        else
+                            gather4(dst, &tm, fb, rc, bar);
                     } else {
                         gather4(dst, &tm, fb, quad, bar);
                     }
@@ -636,7 +640,7 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
              : bw < 64  ? pick(Fa{}, One{})
                         : pick(Fa{}, Two{});
     TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    const int l2hint = l2_hints_requested() ? 1 : 0;
+    const int l2hint = l2_hint_mode();
     k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(tm, a, d, bw, thr, accumulate, err,
                                                        (unsigned long long)wait_limit_ns(), l2hint);
     TCC_CUDA(cudaGetLastError());

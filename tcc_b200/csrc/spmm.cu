@@ -111,14 +111,14 @@ __global__ void hot_hist_kernel(const uint32_t* __restrict__ sketch, uint32_t* _
 
 // One block: the smallest use count K (>= 2) whose rows with count >= K fit
 // kHotRows; stored at hist[kCountBins] (kCountBins = none hot).
-__global__ void hot_threshold_kernel(uint32_t* __restrict__ hist) {
+__global__ void hot_threshold_kernel(uint32_t* __restrict__ hist, uint32_t budget) {
     __shared__ uint32_t done;
     if (threadIdx.x == 0) {
         uint64_t rows = 0;
         uint32_t K = kCountBins;
         for (uint32_t c = kCountBins - 1; c >= 2; --c) {
             rows += hist[c];
-            if (rows > kHotRows) break;
+            if (rows > budget) break;
             K = c;
         }
         hist[kCountBins] = K;
@@ -684,11 +684,17 @@ size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles) {
 }
 
 // TCC_PULL_L2=hot: the bulk-copy pull kernel gives hot rows an evict-last and
-// the others an evict-first L2 priority (the plan then builds the hot mask).
-bool l2_hints_requested() {
+// the others an evict-first L2 priority; TCC_PULL_L2=hub: only the hottest
+// rows (a quarter of the hot budget) get evict-last and the others keep the
+// normal priority.  The plan then builds the hot mask.
+int l2_hint_mode() {
     const char* e = std::getenv("TCC_PULL_L2");
-    return e && std::strcmp(e, "hot") == 0;
+    if (!e) return 0;
+    if (std::strcmp(e, "hot") == 0) return 1;
+    if (std::strcmp(e, "hub") == 0) return 2;
+    return 0;
 }
+bool l2_hints_requested() { return l2_hint_mode() != 0; }
 
 // Work plan of the register-gather kernel in the scratch: chunk descriptors,
 // split windows and a zeroed header (which also clears the error word).
@@ -718,7 +724,7 @@ void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStre
         TCC_CUDA(cudaMemsetAsync(hist, 0, (size_t)kCountBins * 4 + 16, s));
         hot_count_kernel<<<g, 256, 0, s>>>(a.idx, (uint64_t)a.num_tiles * 8, a.num_in, sketch);
         hot_hist_kernel<<<g, 256, 0, s>>>(sketch, hist);
-        hot_threshold_kernel<<<1, 32, 0, s>>>(hist);
+        hot_threshold_kernel<<<1, 32, 0, s>>>(hist, l2_hint_mode() == 2 ? kHotRows / 4 : kHotRows);
         hot_mask_kernel<<<g, 256, 0, s>>>(a.idx, a.num_tiles, a.num_in, sketch, hist,
                                           reinterpret_cast<uint8_t*>(base + L.hot));
     }

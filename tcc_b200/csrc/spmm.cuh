@@ -56,6 +56,7 @@ struct FeatureStore {
 size_t pull_scratch_bytes(uint32_t num_windows, uint32_t num_tiles);
 // TCC_PULL_L2=hot is set: hot-row L2 hints in the bulk-copy pull kernel.
 bool l2_hints_requested();
+int l2_hint_mode();  // 0 none, 1 hot evict-last + cold evict-first, 2 hubs evict-last only
 // Builds the pull work plan in `scratch` on stream s (what plan_ready = 1 reuses).
 void pull_plan(const PullTiles& a, void* scratch, size_t scratch_bytes, cudaStream_t s);
 // keep_plan = false: the caller never passes plan_ready = 1 for this scratch
