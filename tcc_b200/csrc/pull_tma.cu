@@ -63,7 +63,7 @@ constexpr uint32_t kRowPad = 32;                 // bytes between rows beyond th
 constexpr uint32_t kStageBytes = 8 * (kMaxBox * 4 + kRowPad);
 constexpr uint32_t kBatch = 4;                   // tiles per metadata batch (8 lanes each)
 constexpr uint32_t kFlushTiles = 64;             // max tiles summed in one fp32 register chain
-constexpr uint32_t kPieces = 8;                  // tile-range pieces per warp
+constexpr uint32_t kPieces = 8;                  // tile-range pieces per warp (default)
 constexpr unsigned long long kDrainNs = 2000000000ull;  // bound of the drain after a failure
 
 struct __align__(16) StageMeta {
@@ -276,7 +276,7 @@ template <int NP, bool FULL, bool G4>
 __global__ void __launch_bounds__(kTW * 32, 1)
     pull_tma_kernel(const __grid_constant__ CUtensorMap tm, PullTiles a, Dense d, uint32_t bw,
                     uint32_t thr, int accumulate, uint32_t* __restrict__ err,
-                    unsigned long long wait_ns, int l2hint) {
+                    unsigned long long wait_ns, int l2hint, uint32_t pieces) {
     extern __shared__ unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kTW * 32, 1)
     // pieces are spread over the whole matrix, so hub-heavy and
     // many-small-window regions share out evenly across warps
     const uint64_t GW = (uint64_t)gridDim.x * kTW;
-    const uint64_t G = GW * kPieces;
+    const uint64_t G = GW * pieces;
     const uint64_t g0 = (uint64_t)blockIdx.x * kTW + wib;
     const uint32_t T = a.num_tiles, W = a.num_windows;
     const uint32_t* off = a.win_offset;
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(kTW * 32, 1)
 
     bool failed = false;
     uint32_t t = 0, fq = 0, fpar = 0;  // on failure: tile t waited on slot fq, parity fpar
-    for (uint32_t j = 0; j < kPieces && !failed; ++j) {
+    for (uint32_t j = 0; j < pieces && !failed; ++j) {
         const uint64_t piece = g0 + j * GW;
         T0 = (uint32_t)(piece * T / G);
         T1 = (uint32_t)((piece + 1) * T / G);
@@ -604,7 +604,13 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
     const uint32_t bw = d.F <= kMaxBox ? d.F : kMaxBox;
     const uint32_t slices = d.F <= kMaxBox ? 1 : d.F / kMaxBox;
     const uint32_t ctas = (uint32_t)grid_sms();
-    const uint32_t G = ctas * kTW * kPieces;
+    // pieces per warp: TCC_PULL_PIECES (1-64) for measurements, else kPieces
+    uint32_t pieces = kPieces;
+    if (const char* e = std::getenv("TCC_PULL_PIECES")) {
+        const long v = std::strtol(e, nullptr, 10);
+        if (v >= 1 && v <= 64) pieces = (uint32_t)v;
+    }
+    const uint32_t G = ctas * kTW * pieces;
     const bool g4 = use_gather4();
     CUtensorMap tm;
     std::memset(&tm, 0, sizeof(tm));
@@ -642,7 +648,8 @@ void pull_tma(const PullTiles& a, const Dense& d, uint32_t thr, int accumulate, 
     TCC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     const int l2hint = l2_hint_mode();
     k<<<dim3(ctas, slices), kTW * 32, kSmemBytes, s>>>(tm, a, d, bw, thr, accumulate, err,
-                                                       (unsigned long long)wait_limit_ns(), l2hint);
+                                                       (unsigned long long)wait_limit_ns(), l2hint,
+                                                       pieces);
     TCC_CUDA(cudaGetLastError());
 }
 
