@@ -91,7 +91,7 @@ class FeatureStore:
         return self.gpu_shards[0]
 
     def enable_cold_staging(self, budget_bytes: int | None = None, columns: torch.Tensor | None = None,
-                            force_gather: bool = False) -> bool:
+                            force_gather: bool = False, group=None) -> bool:
         """Allocate an HBM staging buffer for the cold rows an aggregation reads,
         if they fit ``budget_bytes`` (default: a quarter of the device's free
         memory).  ``columns``: the column ids the aggregation gathers (e.g. a
@@ -101,10 +101,36 @@ class FeatureStore:
         row instead of one per gather that touches it) and an aggregation reads
         ``cold_stage`` through ``stage_id_map``.  ``force_gather`` stages through
         the row-gather kernel even when every cold row is needed (tests).
-        Returns whether staging is on."""
+
+        ``group`` (a process group of the ranks that hold this same store, one
+        per GPU): cooperative staging -- the cold block is cut into one
+        contiguous chunk per rank, each rank copies only its chunk over PCIe and
+        an all-gather over NVLink assembles the whole block on every rank, so
+        each cold row crosses the host link once per call for the whole job
+        instead of once per rank (the GPUs of a box share the host's memory
+        bandwidth).  Returns whether staging is on."""
         if self.n_cold == 0:
             return False
         device = self.device
+        self.stage_group = None
+        if group is not None and torch.distributed.get_world_size(group) > 1:
+            world = torch.distributed.get_world_size(group)
+            rank = torch.distributed.get_rank(group)
+            chunk = (self.n_cold + world - 1) // world
+            if budget_bytes is None:
+                free, _ = torch.cuda.mem_get_info(device)
+                budget_bytes = free // 4
+            if (world + 1) * chunk * self.F * 4 > budget_bytes:
+                return False
+            self.stage_group = group
+            self.cold_stage = torch.empty((world * chunk, self.F), dtype=torch.float32,
+                                          device=device)
+            self.stage_chunk = torch.empty((chunk, self.F), dtype=torch.float32, device=device)
+            r0, r1 = min(rank * chunk, self.n_cold), min((rank + 1) * chunk, self.n_cold)
+            self.stage_rows = (r0, r1)
+            self.stage_ids = None
+            self.stage_id_map = self.id_map  # every cold row, the host block's order
+            return True
         ids = stage_map = None
         if columns is not None:
             c, ids, stage_map = cold_stage_plan(columns.to(device), self.cache_search_map, self.id_map,
@@ -129,7 +155,18 @@ class FeatureStore:
     def stage_cold(self, stream: torch.cuda.Stream) -> None:
         """Bring the staged cold rows from pinned host memory into ``cold_stage``
         on ``stream`` (async): one bulk copy when every cold row is staged, else
-        the row-gather kernel reading the host rows zero-copy."""
+        the row-gather kernel reading the host rows zero-copy; with cooperative
+        staging, this rank's chunk over PCIe and an all-gather of the chunks
+        (``stream`` then waits for the all-gather)."""
+        if getattr(self, "stage_group", None) is not None:
+            r0, r1 = self.stage_rows
+            with torch.cuda.stream(stream):
+                if r1 > r0:
+                    self.stage_chunk[:r1 - r0].copy_(self.cpu_rows[r0:r1], non_blocking=True)
+                work = torch.distributed.all_gather_into_tensor(
+                    self.cold_stage, self.stage_chunk, group=self.stage_group, async_op=True)
+                work.wait()  # the stream waits for the gathered block
+            return
         if self.stage_ids is None:
             with torch.cuda.stream(stream):
                 self.cold_stage.copy_(self.cpu_rows, non_blocking=True)

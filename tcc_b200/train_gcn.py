@@ -152,8 +152,22 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
     # stream (the copy for epoch e + 1 overlaps the rest of epoch e), or read
     # zero-copy from pinned host memory by every gather that touches them
     store = R["store"]
+    # more than one GPU: the ranks stage the cold block cooperatively (each
+    # copies a chunk over PCIe, an all-gather on its own communicator, so it
+    # does not queue behind the halo exchanges, assembles the rest)
+    stage_group = None
+    if world > 1 and bool(cfg.get("cold_stage_coop", True)):
+        stage_group = dist.new_group(backend="nccl", pg_options=nccl_options())
     staged = bool(cfg.get("cold_staging", True)) and store.enable_cold_staging(
-        columns=R["tiles_g"].sparseIdx, force_gather=bool(cfg.get("cold_stage_gather", False)))
+        columns=R["tiles_g"].sparseIdx, force_gather=bool(cfg.get("cold_stage_gather", False)),
+        group=stage_group)
+    if stage_group is not None:
+        # cooperative staging runs collectives: every rank stages, or none does
+        agree = torch.tensor([1 if staged else 0], device=device)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+        staged = bool(agree.item())
+        if not staged:
+            store.stage_group = None
     if staged:
         side = torch.cuda.Stream(device=device)
         # the staging buffer and its row ids were made on the current stream
@@ -162,6 +176,8 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
         store.cold_stage.record_stream(side)  # written on the side stream
         if store.stage_ids is not None:
             store.stage_ids.record_stream(side)  # read on the side stream
+        if getattr(store, "stage_chunk", None) is not None:
+            store.stage_chunk.record_stream(side)  # the rank's chunk, written on the side stream
         ready = torch.cuda.Event()
         used = torch.cuda.Event()
         store.stage_cold(side)

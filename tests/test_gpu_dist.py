@@ -97,3 +97,51 @@ def test_row_partitioned_spmm_matches_single_gpu(gpu):
     for rank, err, halo in res:
         assert err <= FP32_TOL, (rank, err)
         assert halo > 0
+
+
+def _gcn_worker(rank, world, port, cfg, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    from tcc_b200.partition import nccl_options
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), pg_options=nccl_options(),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from tcc_b200 import train_gcn
+        r = train_gcn.train(cfg, torch.device("cuda", rank), world, rank)
+        torch.cuda.synchronize()
+        if rank == 0:
+            q.put((r["losses"], r["cold_staging"]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
+def test_gcn_training_across_gpus_matches_one_gpu(gpu):
+    """The row-partitioned GCN trainer (layer-2 halo exchange, gradient
+    all-reduce, cold rows staged cooperatively: each rank copies a chunk of the
+    cold block over PCIe and an all-gather assembles the rest) follows the
+    one-GPU loss trajectory (dropout off, so only summation order differs)."""
+    from tcc_b200 import train_gcn
+    cfg = train_gcn.config(shrink=5)
+    cfg["dropout"] = 0.0
+    cfg["epochs"] = 4
+    one = train_gcn.train(dict(cfg), torch.device("cuda", 0), 1, 0)["losses"]
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gcn_worker, args=(r, world, port, dict(cfg), q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    losses, staged = q.get(timeout=10)
+    assert staged
+    assert max(abs(a - b) / b for a, b in zip(losses, one)) < 1e-3, (losses, one)
