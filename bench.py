@@ -84,6 +84,10 @@ def parse():
     p.add_argument("--dist-mode", choices=["exchange", "replicated"], default="exchange",
                    help="N > 1: 'exchange' = rows, X and G split across GPUs, the feature "
                         "halo exchanged every SpMM; 'replicated' = X and G resident on every GPU")
+    p.add_argument("--transport", choices=["auto", "peer", "nccl"], default="auto",
+                   help="exchange mode's halo transport: 'peer' = one kernel stores the rows "
+                        "into the receivers' HBM over NVLink (CUDA IPC); 'nccl' = packed rows, "
+                        "one NCCL all-to-all; 'auto' = peer when every GPU pair has peer access")
     p.add_argument("--workload", choices=["spmm", "gcn4", "config5"], default="spmm",
                    help="spmm: the config-2 SpMM step (headline); gcn4: config-4 GCN epoch time "
                         "(tcc_b200.train_gcn, epochs = --steps); config5: the scale-26 forward "
@@ -386,7 +390,7 @@ def run_ours(args, rank, world, local_rank):
     halo_rows = 0
     if mode == "exchange":
         dg = DistGraph(lrp, lcol, bounds, rs_local=s[r0:r1].contiguous(), cs_global=s,
-                       tc_threshold=thr)
+                       tc_threshold=thr, transport=args.transport)
         halo_rows = dg.halo_rows
         X_loc, G_loc = X_loc.contiguous(), G_loc.contiguous()
 
@@ -395,7 +399,9 @@ def run_ours(args, rank, world, local_rank):
 
         fwd_pass = lambda Xd, Yd: dg.spmm(Xd, Yd)  # noqa: E731
         bwd_pass = fwd_pass  # A symmetric: the rank's rows of A^T are its rows of A
-        launches_per_step = 2 * 4  # per SpMM: pack, zero + pull (local), pull (halo)
+        # per SpMM -- peer: push, zero + pull (local), wait, pull (halo), release,
+        # and the timer's arrival wait; nccl: pack, zero + pull (local), pull (halo)
+        launches_per_step = 2 * (7 if dg.transport == "peer" else 4)
     else:
         tl = full_bcsr if world == 1 else T.from_csr(lrp, lcol, n_loc, n, kind="bcsr")
         crp, ccol = (rowptr, col) if world == 1 else column_block(rowptr, col, r0, r1)
@@ -447,6 +453,9 @@ def run_ours(args, rank, world, local_rank):
     mx = allreduce([ms, fwd_ms, bwd_ms] + ([phases[k] for k in sorted(phases)] if phases else []),
                    dist.ReduceOp.MAX if world > 1 else None, device)
     ms, fwd_ms_max, bwd_ms_max = mx[:3]
+    if mode == "exchange":  # the two passes interleave (local, local, halo, halo): half a step each
+        fwd_ms = bwd_ms = ms / args.steps / 2
+        fwd_ms_max = bwd_ms_max = ms / args.steps / 2
     if phases:
         phases = {k: round(v, 4) for k, v in zip(sorted(phases), mx[3:])}
     tot = allreduce([float(nnz_loc), float(halo_rows)], dist.ReduceOp.SUM if world > 1 else None,
@@ -492,6 +501,13 @@ def run_ours(args, rank, world, local_rank):
     # the same outputs as the device-resident run (split windows reduce in any order)
     e2e_ok = all(((a - b).abs().max() / b.abs().max().clamp(min=1e-30)).item() <= 1e-5
                  for a, b in ((hY, Y.cpu()), (hZ, Z.cpu())))
+    transport = "none"
+    if mode == "exchange":
+        transport = dg.transport
+        dev_err = dg.device_error()
+        dg.close()  # collective: every rank, before rank 0 reports
+        if dev_err:
+            raise RuntimeError(f"halo exchange device error {dev_err}")
 
     if rank != 0:
         return
@@ -521,9 +537,13 @@ def run_ours(args, rank, world, local_rank):
                    "tc_threshold": thr, "l2": "inputs larger than L2 (X, G 512 MiB)",
                    "parallelism": ("1 GPU" if world == 1 else
                                    f"{world}-way 1D row partition balanced by tiles; " +
-                                   ("compacted feature halo all-to-all over NCCL each SpMM, "
-                                    "overlapped with the local tiles" if mode == "exchange" else
-                                    "X, G resident on every GPU")),
+                                   (("compacted feature halo stored into the receivers' HBM "
+                                     "over NVLink by one gather kernel (CUDA IPC peer memory)"
+                                     if transport == "peer" else
+                                     "compacted feature halo all-to-all over NCCL") +
+                                    " each SpMM, overlapped with the local tiles"
+                                    if mode == "exchange" else "X, G resident on every GPU")),
+                   "transport": transport,
                    "row_bounds": bounds if world > 1 else None,
                    "gen_s": round(gen_s, 3), "convert_s": round(conv_s, 3)},
         "parity": {"checker": "fp64 torch recomputation of sampled output rows (device gathers "
@@ -873,7 +893,8 @@ def run_config5(args, rank, world, local_rank):
         def spmm():
             T.bcsr_spmm(tl, Xfull, Y, tc_threshold=args.tc_threshold, rs=rs)
     else:
-        dg = DistGraph(lrp, lcol, bounds, rs_local=rs, cs_global=None, tc_threshold=args.tc_threshold)
+        dg = DistGraph(lrp, lcol, bounds, rs_local=rs, cs_global=None, tc_threshold=args.tc_threshold,
+                       transport=args.transport)
         del lcol
         torch.cuda.empty_cache()
         torch.cuda.synchronize()
@@ -909,6 +930,12 @@ def run_config5(args, rank, world, local_rank):
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
     ms = t.item()
     nnz_total, halo_total = tot.tolist()
+    transport = getattr(dg, "transport", "none")
+    if hasattr(dg, "close"):
+        dev_err = dg.device_error()
+        dg.close()  # collective: every rank
+        if dev_err:
+            raise RuntimeError(f"halo exchange device error {dev_err}")
     if rank != 0:
         return
     peak, peak_kind = measured_peaks()
@@ -927,8 +954,9 @@ def run_config5(args, rank, world, local_rank):
                    "halo_rows_total": int(halo_total), "tc_threshold": args.tc_threshold,
                    "parallelism": (f"{world}-way 1D row partition, " +
                                    ("X all-gathered once at set-up (static input features)"
-                                    if replicated else "halo exchanged every step"))
+                                    if replicated else f"halo exchanged every step ({transport})"))
                    if world > 1 else "1 GPU",
+                   "transport": transport,
                    "allgather_s": None if allgather_s is None else round(allgather_s, 3),
                    "gen_s": round(gen_s, 2), "convert_s": round(conv_s, 2)},
         "roofline": {"bound": "hbm", "achieved": round(achieved / world, 1), "peak": peak,
@@ -936,7 +964,8 @@ def run_config5(args, rank, world, local_rank):
                      "traffic": None, "kernel": "forward SpMM (exchange + local + halo tiles)",
                      "peak_kind": peak_kind},
         "e2e": None,
-        "gpu_launches": args.steps * (2 if world == 1 or replicated else 5),
+        "gpu_launches": args.steps * (2 if world == 1 or replicated else
+                                      6 if transport == "peer" else 5),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

@@ -274,6 +274,64 @@ tcc_status tcc_scatter_add_rows(const float* in, uint64_t ldi, const int64_t* id
                                 float* out, uint64_t ldo, uint64_t num_rows, uint32_t F,
                                 uint32_t* bad_flag, cudaStream_t stream);
 
+/* ------------------------------------------- halo exchange over NVLink ---- */
+/* No counterpart in the reference, whose multi-GPU path reads peer feature
+ * caches inside the SpMM kernel (cnic/src/core/spmm_kernel.cu:145-147).  The
+ * row-partitioned SpMM's halo exchange through peer memory, one process per
+ * GPU of one box: each rank allocates its receive buffers and one flag block
+ * with tcc_peer_alloc, the ranks swap the IPC handles (any host channel) and
+ * map each other's with tcc_peer_open.  Per exchange (tag t, step number s,
+ * counted the same on every rank, starting at 1):
+ *   sender:   tcc_halo_push -- gathers its rows and stores them into the
+ *             receivers' buffers over NVLink, then marks them arrived;
+ *   receiver: tcc_halo_wait -- the stream continues once every sender's rows
+ *             of step s arrived; the kernels after it read the buffer;
+ *             tcc_halo_release after the last of them -- the senders may
+ *             overwrite the buffer with step s + 1.
+ * Every wait is bounded by wait_ns (%globaltimer); on expiry the kernel
+ * records TCC_DEVERR_WAIT_TIMEOUT in the flag block, writes no rows, and
+ * returns.  Read the word with tcc_peer_device_error (synchronises).  No
+ * multicast is involved. */
+#define TCC_PEER_MAX_RANKS 8
+#define TCC_PEER_MAX_TAGS 4
+#define TCC_PEER_FLAGS_BYTES 4096
+typedef struct tcc_ipc_handle {
+    unsigned char bytes[64]; /* a cudaIpcMemHandle_t */
+} tcc_ipc_handle;
+
+/* cudaMalloc + zero fill + cudaIpcGetMemHandle (synchronises). */
+tcc_status tcc_peer_alloc(size_t bytes, void** ptr, tcc_ipc_handle* handle);
+/* Map another process's tcc_peer_alloc buffer into this one (peer access
+ * enabled lazily); tcc_peer_close unmaps it, tcc_peer_free frees one's own
+ * (after every peer closed its mapping). */
+tcc_status tcc_peer_open(const tcc_ipc_handle* handle, void** ptr);
+tcc_status tcc_peer_close(void* mapped);
+tcc_status tcc_peer_free(void* ptr);
+
+typedef struct tcc_halo_push_args {
+    const float* x;          /* this rank's rows [num_rows x width], stride ldx */
+    uint64_t ldx, num_rows;
+    const int64_t* send_idx; /* rows to send, grouped by receiver */
+    uint32_t width, world, rank, tag, seq;
+    uint32_t max_blocks;     /* grid cap (0: 8 CTAs per SM) */
+    uint64_t seg[TCC_PEER_MAX_RANKS + 1]; /* send_idx[seg[p]:seg[p+1]] go to rank p */
+    float* dst[TCC_PEER_MAX_RANKS];       /* rank p's receive rows for this rank (mapped) */
+    uint64_t ld_dst;                      /* their row stride (floats) */
+    void* peer_flags[TCC_PEER_MAX_RANKS]; /* rank p's flag block (mapped) */
+    void* flags;                          /* this rank's flag block */
+    uint64_t wait_ns;                     /* bound of the wait for step seq-1's release */
+} tcc_halo_push_args;
+
+tcc_status tcc_halo_push(const tcc_halo_push_args* args, cudaStream_t stream);
+/* peer_mask: bit p set when rank p sends rows to this rank. */
+tcc_status tcc_halo_wait(void* flags, uint32_t tag, uint32_t seq, uint32_t peer_mask,
+                         uint64_t wait_ns, cudaStream_t stream);
+/* peer_flags[p]: rank p's mapped flag block; peer_mask: the senders. */
+tcc_status tcc_halo_release(void* const* peer_flags, uint32_t world, uint32_t rank, uint32_t tag,
+                            uint32_t seq, uint32_t peer_mask, cudaStream_t stream);
+/* The flag block's device error word (TCC_DEVERR_*; synchronises `stream`). */
+tcc_status tcc_peer_device_error(void* flags, int* code, cudaStream_t stream);
+
 /* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
  * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):
  * C[num_rows x F] = diag(rs) * A * diag(cs) * B[num_cols x F]; row windows own

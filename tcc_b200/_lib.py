@@ -49,6 +49,27 @@ class Swtcf(C.Structure):
                 ("fwd_plan_bytes", C.c_uint64), ("fwd_plan_ready", C.c_int32)]
 
 
+PEER_MAX_RANKS = 8    # TCC_PEER_MAX_RANKS
+PEER_MAX_TAGS = 4     # TCC_PEER_MAX_TAGS
+PEER_FLAGS_BYTES = 4096  # TCC_PEER_FLAGS_BYTES
+
+
+class IpcHandle(C.Structure):
+    """tcc_ipc_handle (a cudaIpcMemHandle_t, 64 bytes)."""
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
+class HaloPushArgs(C.Structure):
+    """tcc_halo_push_args."""
+    _fields_ = [("x", C.c_void_p), ("ldx", C.c_uint64), ("num_rows", C.c_uint64),
+                ("send_idx", C.c_void_p), ("width", C.c_uint32), ("world", C.c_uint32),
+                ("rank", C.c_uint32), ("tag", C.c_uint32), ("seq", C.c_uint32),
+                ("max_blocks", C.c_uint32), ("seg", C.c_uint64 * (PEER_MAX_RANKS + 1)),
+                ("dst", C.c_void_p * PEER_MAX_RANKS), ("ld_dst", C.c_uint64),
+                ("peer_flags", C.c_void_p * PEER_MAX_RANKS), ("flags", C.c_void_p),
+                ("wait_ns", C.c_uint64)]
+
+
 class Bcsr(C.Structure):
     """Field-for-field tcc_bcsr / the reference's BCSR<float>."""
     _fields_ = [("num_rows", C.c_uint32), ("num_cols", C.c_uint32), ("nnz", C.c_uint32),
@@ -107,6 +128,14 @@ PROTOTYPES = {
                                     _i, _vp]),
     "tcc_noalloc_device_error": (_st, [C.POINTER(_i), _vp]),
     "tcc_scatter_add_rows": (_st, [_vp, _u64, _vp, _u64, _vp, _u64, _u64, _u32, _vp, _vp]),
+    "tcc_peer_alloc": (_st, [C.c_size_t, C.POINTER(_vp), C.POINTER(IpcHandle)]),
+    "tcc_peer_open": (_st, [C.POINTER(IpcHandle), C.POINTER(_vp)]),
+    "tcc_peer_close": (_st, [_vp]),
+    "tcc_peer_free": (_st, [_vp]),
+    "tcc_halo_push": (_st, [C.POINTER(HaloPushArgs), _vp]),
+    "tcc_halo_wait": (_st, [_vp, _u32, _u32, _u32, _u64, _vp]),
+    "tcc_halo_release": (_st, [C.POINTER(_vp), _u32, _u32, _u32, _u32, _u32, _vp]),
+    "tcc_peer_device_error": (_st, [_vp, C.POINTER(_i), _vp]),
     "tcc_relu_dropout_forward": (_st, [_vp, _vp, _u64, C.c_float, _u64, _vp]),
     "tcc_relu_dropout_backward": (_st, [_vp, _vp, _vp, _u64, C.c_float, _vp]),
     "tcc_bcsr_spmm_t": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),

@@ -514,6 +514,44 @@ tcc_status tcc_scatter_add_rows(const float* in, uint64_t ldi, const int64_t* id
     });
 }
 
+tcc_status tcc_peer_alloc(size_t bytes, void** ptr, tcc_ipc_handle* handle) {
+    static_assert(sizeof(tcc_ipc_handle) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+    return guarded("tcc_peer_alloc", [&] { tcc::peer_alloc(bytes, ptr, handle); });
+}
+
+tcc_status tcc_peer_open(const tcc_ipc_handle* handle, void** ptr) {
+    return guarded("tcc_peer_open", [&] { tcc::peer_open(handle, ptr); });
+}
+
+tcc_status tcc_peer_close(void* mapped) {
+    return guarded("tcc_peer_close", [&] { tcc::peer_close(mapped); });
+}
+
+tcc_status tcc_peer_free(void* ptr) {
+    return guarded("tcc_peer_free", [&] { tcc::peer_free(ptr); });
+}
+
+tcc_status tcc_halo_push(const tcc_halo_push_args* args, cudaStream_t stream) {
+    return guarded("tcc_halo_push", [&] { tcc::halo_push(args, stream); });
+}
+
+tcc_status tcc_halo_wait(void* flags, uint32_t tag, uint32_t seq, uint32_t peer_mask,
+                         uint64_t wait_ns, cudaStream_t stream) {
+    return guarded("tcc_halo_wait",
+                   [&] { tcc::halo_wait(flags, tag, seq, peer_mask, wait_ns, stream); });
+}
+
+tcc_status tcc_halo_release(void* const* peer_flags, uint32_t world, uint32_t rank, uint32_t tag,
+                            uint32_t seq, uint32_t peer_mask, cudaStream_t stream) {
+    return guarded("tcc_halo_release", [&] {
+        tcc::halo_release(peer_flags, world, rank, tag, seq, peer_mask, stream);
+    });
+}
+
+tcc_status tcc_peer_device_error(void* flags, int* code, cudaStream_t stream) {
+    return guarded("tcc_peer_device_error", [&] { tcc::peer_device_error(flags, code, stream); });
+}
+
 tcc_status tcc_relu_dropout_forward(const float* in, float* out, uint64_t n, float p,
                                     uint64_t seed, cudaStream_t stream) {
     return guarded("tcc_relu_dropout_forward", [&] {

@@ -63,7 +63,7 @@ constexpr uint32_t kRowPad = 32;                 // bytes between rows beyond th
 constexpr uint32_t kStageBytes = 8 * (kMaxBox * 4 + kRowPad);
 constexpr uint32_t kBatch = 4;                   // tiles per metadata batch (8 lanes each)
 constexpr uint32_t kFlushTiles = 64;             // max tiles summed in one fp32 register chain
-constexpr uint32_t kPieces = 8;                  // tile-range pieces per warp (default)
+constexpr uint32_t kPieces = 12;                 // tile-range pieces per warp (default; 4-24 measured)
 constexpr unsigned long long kDrainNs = 2000000000ull;  // bound of the drain after a failure
 
 struct __align__(16) StageMeta {

@@ -78,6 +78,17 @@ void pull_umma(const PullTiles& a, const Dense& d, int accumulate, uint32_t* err
 void scatter_add_rows(const float* in, uint64_t ldi, const int64_t* idx, uint64_t n, float* out,
                       uint64_t ldo, uint64_t num_rows, uint32_t F, uint32_t* bad, cudaStream_t s);
 // rows.cu: out[i] = X[idx[i]] (halo pack of the row-partitioned SpMM).
+// peer.cu: the halo exchange over NVLink peer memory
+void peer_alloc(size_t bytes, void** ptr, void* handle);
+void peer_open(const void* handle, void** ptr);
+void peer_close(void* mapped);
+void peer_free(void* ptr);
+void halo_push(const tcc_halo_push_args* a, cudaStream_t s);
+void halo_wait(void* flags, uint32_t tag, uint32_t seq, uint32_t mask, unsigned long long wait_ns,
+               cudaStream_t s);
+void halo_release(void* const* peer_flags, uint32_t world, uint32_t rank, uint32_t tag,
+                  uint32_t seq, uint32_t mask, cudaStream_t s);
+void peer_device_error(void* flags, int* code, cudaStream_t s);
 void gather_rows(const float* X, uint64_t ldx, uint64_t num_rows, const int64_t* idx, uint64_t n,
                  float* out, uint64_t ldo, uint32_t F, uint32_t* bad, cudaStream_t s);
 // gcn_ops.cu: fused ReLU + dropout of a GCN hidden layer and its backward.

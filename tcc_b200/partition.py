@@ -7,12 +7,16 @@ of remote columns; the halo is compacted to the distinct remote columns, and
 each owner learns once, at set-up, which of its rows every peer needs.
 
 One SpMM step on rank g:
-  1. on a high-priority side stream, pack the rows peers need (the
-     tcc_gather_rows kernel) and start an NCCL all-to-all (uneven splits, one
-     message per peer pair);
+  1. on a high-priority side stream, send the rows peers need: with the peer
+     transport (the default when every pair of GPUs has peer access), one
+     kernel gathers them and stores them straight into the receivers' halo
+     buffers over NVLink (tcc_b200.peer); with the NCCL transport, the
+     tcc_gather_rows kernel packs them and an NCCL all-to-all (uneven splits)
+     moves them;
   2. meanwhile run the local-column tiles on the caller's stream:
      Y = A_loc · X[P_g];
-  3. wait for the halo, then Y += A_halo · X_halo.
+  3. wait for the halo, then Y += A_halo · X_halo (and, with the peer
+     transport, hand the halo buffer back to the senders).
 A_loc and A_halo are BCSR tilings of the local rows with column ids remapped to
 [0, |P_g|) and [0, |halo|).  The process group should give NCCL high-priority
 streams (ProcessGroupNCCL.Options.is_high_priority_stream) so the exchange's
@@ -85,7 +89,7 @@ class DistGraph:
 
     def __init__(self, rowptr: torch.Tensor, col: torch.Tensor, bounds: list, group=None,
                  rs_local=None, cs_global=None, tc_threshold: int = 12, build_tiles: bool = True,
-                 symmetric: bool = False):
+                 symmetric: bool = False, transport: str = "auto"):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -139,6 +143,20 @@ class DistGraph:
         self.symmetric = symmetric
         self.tiles_loc = self.tiles_halo = None
         self.tiles_loc_t = self.tiles_halo_t = None  # BCSC tilings, built by the first spmm_t
+        # halo transport of the forward exchange: "peer" (rows stored into the
+        # receivers' HBM over NVLink by one kernel, tcc_b200.peer) or "nccl"
+        # (packed rows, one all-to-all); "auto" takes peer when every pair of
+        # the ranks' GPUs has peer access
+        self.peer = None
+        if transport not in ("auto", "peer", "nccl"):
+            raise ValueError("transport must be auto, peer or nccl")
+        if self.world > 1 and rowptr.is_cuda and transport != "nccl":
+            from .peer import PeerExchange, peers_reachable
+            if peers_reachable(group):
+                self.peer = PeerExchange(group, self.send_idx, self.send_counts, self.recv_counts)
+            elif transport == "peer":
+                raise RuntimeError("transport='peer' needs peer access between every pair of GPUs")
+        self.transport = "peer" if self.peer is not None else ("nccl" if self.world > 1 else "none")
         if build_tiles:
             from . import tiles
             self.tiles_loc = tiles.from_csr(self.loc_rowptr, self.loc_col, self.n_local,
@@ -173,6 +191,8 @@ class DistGraph:
         The halo buffer (one per ``tag`` and width) is reused by the next
         exchange with the same tag.  ``timer``: a dict that receives CUDA
         events "pack{tag}" (rows packed) and "xchg{tag}" (halo arrived)."""
+        if self.peer is not None:
+            return self._peer_exchange(X_local, async_op, tag, timer)
         recv = self._buf(f"recv{tag}", self.halo_rows, X_local)
         if self.world == 1:
             return recv, None
@@ -203,6 +223,37 @@ class DistGraph:
             work = None
         return recv, work
 
+    def _peer_exchange(self, X_local, async_op, tag, timer):
+        from .peer import PeerWork
+        recv = self.peer.recv_buffer(tag, X_local.shape[1])
+        main = torch.cuda.current_stream(X_local.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=X_local.device, priority=-1)
+        side = self._side
+        side.wait_stream(main)
+        seq = self.peer.push(X_local, tag, side)
+        if timer is not None:
+            timer[f"pack{tag}"] = _event(side)  # this rank's rows stored at the receivers
+        work = PeerWork(self.peer, tag, seq, X_local.device)
+        if timer is not None:  # the arrival, seen from a stream nothing else waits on
+            if self._tstream is None:
+                self._tstream = torch.cuda.Stream(device=X_local.device)
+            self.peer.wait(tag, seq, self._tstream)
+            timer[f"xchg{tag}"] = _event(self._tstream)
+        if not async_op:
+            work.wait(main)
+        return recv, work
+
+    def device_error(self) -> int:
+        """The peer transport's device error word (0 when none, or with NCCL)."""
+        return self.peer.device_error() if self.peer is not None else 0
+
+    def close(self):
+        """Collective: release the peer transport's mapped buffers."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
     def _local(self, X_local, out, reserve):
         from . import tiles
         from . import _lib as L
@@ -219,18 +270,19 @@ class DistGraph:
     def _halo(self, halo, work, Y, reserve=False):
         from . import tiles
         from . import _lib as L
-        if work is not None:
+        if work is not None and not getattr(work, "waited", False):
             work.wait()
-        if self.tiles_halo is None:
-            return
-        prev = L.lib().tcc_get_grid_reserve()
-        L.lib().tcc_set_grid_reserve(self.comm_sms if reserve else 0)
-        try:
-            with torch.cuda.nvtx.range("tcc.halo_tiles"):
-                tiles.bcsr_spmm(self.tiles_halo, halo, Y, tc_threshold=self.tc_threshold,
-                                rs=self.rs, cs=self.cs_halo, accumulate=True)
-        finally:
-            L.lib().tcc_set_grid_reserve(prev)
+        if self.tiles_halo is not None:
+            prev = L.lib().tcc_get_grid_reserve()
+            L.lib().tcc_set_grid_reserve(self.comm_sms if reserve else 0)
+            try:
+                with torch.cuda.nvtx.range("tcc.halo_tiles"):
+                    tiles.bcsr_spmm(self.tiles_halo, halo, Y, tc_threshold=self.tc_threshold,
+                                    rs=self.rs, cs=self.cs_halo, accumulate=True)
+            finally:
+                L.lib().tcc_set_grid_reserve(prev)
+        if hasattr(work, "release"):  # peer transport: the senders may reuse the buffer
+            work.release()
 
     def spmm(self, X_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """Y[P_g] = (diag(rs) A diag(cs) X)[P_g], exchange overlapped with the
@@ -245,10 +297,12 @@ class DistGraph:
     def spmm_pair(self, X_local: torch.Tensor, Y: torch.Tensor, G_local: torch.Tensor,
                   Z: torch.Tensor, timer: dict | None = None):
         """Two SpMMs over the partition, Y = Â[P_g, :]·X and Z = Â[P_g, :]·G,
-        with both halo exchanges queued back to back at the start, so G's halo
-        travels while X's tiles run.  ``timer``: a dict that receives CUDA
-        events -- "start", "pack0/1", "xchg0/1" (halos arrived), "local0/1"
-        (local tiles done) and "done0/1" (Y, Z complete)."""
+        with both halo exchanges queued back to back at the start and both
+        local passes run before either halo pass, so the halos travel while
+        the local tiles (which need nothing remote) run.  ``timer``: a dict
+        that receives CUDA events -- "start", "pack0/1", "xchg0/1" (halos
+        arrived), "local0/1" (local tiles of Y / Z done) and "done0/1" (Y, Z
+        complete)."""
         main = torch.cuda.current_stream(X_local.device)
         if timer is not None:
             timer["start"] = _event(main)
@@ -259,12 +313,12 @@ class DistGraph:
         self._local(X_local, Y, reserve=comm)
         if timer is not None:
             timer["local0"] = _event(main)
-        self._halo(hx, wx, Y, reserve=comm)  # G's rows are still on the wire
-        if timer is not None:
-            timer["done0"] = _event(main)
-        self._local(G_local, Z, reserve=comm)
+        self._local(G_local, Z, reserve=comm)  # the halos are still on the wire
         if timer is not None:
             timer["local1"] = _event(main)
+        self._halo(hx, wx, Y, reserve=comm)
+        if timer is not None:
+            timer["done0"] = _event(main)
         self._halo(hg, wg, Z)
         if timer is not None:
             timer["done1"] = _event(main)

@@ -253,7 +253,13 @@ def train(cfg: dict, device, world: int, rank: int, transform_first: bool | None
     if world > 1:
         dist.all_reduce(nnz)
         dist.all_reduce(halo)
-    return dict(epoch_s=t.tolist(), losses=losses, nnz=float(nnz), halo_rows=float(halo),
+    transport = R["dg"].transport
+    dev_err = R["dg"].device_error()
+    R["dg"].close()  # collective: every rank
+    if dev_err:
+        raise RuntimeError(f"halo exchange device error {dev_err}")
+    return dict(transport=transport, cold_coop=getattr(R["store"], "stage_group", None) is not None,
+                epoch_s=t.tolist(), losses=losses, nnz=float(nnz), halo_rows=float(halo),
                 gen_s=R["gen_s"], conv_s=R["conv_s"], store_hot=R["store"].n_hot,
                 store_cold=R["store"].n_cold, cold_staging=staged, transform_first=transform_first)
 
@@ -308,9 +314,13 @@ def main(argv=None):
                 "config": {"workload": "config4", "nodes": cfg["nodes"], "nnz": int(r["nnz"]),
                            "F_in": cfg["F_in"], "hidden": cfg["hidden"], "classes": cfg["classes"],
                            "hot_rows": r["store_hot"], "cold_rows": r["store_cold"],
-                           "cold_rows_path": ("pinned host -> HBM staging buffer, one bulk copy per "
-                                              "epoch on a side stream (overlapped)" if r["cold_staging"]
+                           "cold_rows_path": (("pinned host -> HBM staging buffer once per epoch on "
+                                               "a side stream (overlapped)" +
+                                               ("; a chunk per rank over PCIe, then an NCCL "
+                                                "all-gather" if r.get("cold_coop") else ""))
+                                              if r["cold_staging"]
                                               else "zero-copy reads of pinned host memory"),
+                           "halo_transport": r["transport"],
                            "halo_rows_total": int(r["halo_rows"]), "transform_first": r["transform_first"],
                            "order": "layer 1 from the hot/cold store, layer 2 over the row partition"}}),
                   flush=True)

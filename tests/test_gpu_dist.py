@@ -1,6 +1,8 @@
-"""Row-partitioned SpMM over NCCL: every rank's rows equal the single-GPU
-result -- the forward pass, the pipelined pair the bench times, and the
-transposed pass of a directed graph (partial rows returned to their owners).
+"""Row-partitioned SpMM across GPUs: every rank's rows equal the single-GPU
+result -- the forward pass, the pipelined pair the bench times (several steps,
+new operands each, so a halo buffer is reused only after its readers released
+it), and the transposed pass of a directed graph (partial rows returned to
+their owners) -- with the halo moved by the peer-memory transport and by NCCL.
 Spawns one process per visible GPU (2 or more); skipped otherwise."""
 import os
 import socket
@@ -22,7 +24,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, transport, q):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -45,7 +47,9 @@ def _worker(rank, world, port, q):
         r0, r1 = bounds[rank], bounds[rank + 1]
         dg = DistGraph((rowptr[r0:r1 + 1] - rowptr[r0]).contiguous(),
                        col[rowptr[r0]:rowptr[r1]].contiguous(), bounds,
-                       rs_local=s[r0:r1].contiguous(), cs_global=s, tc_threshold=65)
+                       rs_local=s[r0:r1].contiguous(), cs_global=s, tc_threshold=65,
+                       transport=transport)
+        assert dg.transport == transport
         gen = torch.Generator(device=dev)
         gen.manual_seed(3)
         X = torch.randn((deg.numel(), 64), generator=gen, device=dev)  # same X on every rank
@@ -53,13 +57,17 @@ def _worker(rank, world, port, q):
         full = tiles.from_csr(rowptr, col, deg.numel(), deg.numel(), kind="bcsr")
         Yref = tiles.bcsr_spmm(full, X, tc_threshold=65, rs=s, cs=s)[r0:r1]
         err = (torch.linalg.norm(Y - Yref) / torch.linalg.norm(Yref)).item()
-        # the pipelined pair of the bench's step (A symmetric: Z = A[P_g, :] G)
+        # the pipelined pair of the bench's step (A symmetric: Z = A[P_g, :] G),
+        # four steps back to back with new operands, checked after each
         Gm = torch.randn((deg.numel(), 64), generator=gen, device=dev)
-        Y2, Z2 = torch.empty_like(Y), torch.empty_like(Y)
-        dg.spmm_pair(X[r0:r1].contiguous(), Y2, Gm[r0:r1].contiguous(), Z2)
         Zref = tiles.bcsr_spmm(full, Gm, tc_threshold=65, rs=s, cs=s)[r0:r1]
-        err = max(err, (torch.linalg.norm(Y2 - Yref) / torch.linalg.norm(Yref)).item(),
-                  (torch.linalg.norm(Z2 - Zref) / torch.linalg.norm(Zref)).item())
+        Y2, Z2 = torch.empty_like(Y), torch.empty_like(Y)
+        for step in range(4):
+            a, b = float(step + 1), float(1 - 2 * (step & 1))
+            dg.spmm_pair((a * X[r0:r1]).contiguous(), Y2, (b * Gm[r0:r1]).contiguous(), Z2)
+            err = max(err, (torch.linalg.norm(Y2 - a * Yref) / torch.linalg.norm(a * Yref)).item(),
+                      (torch.linalg.norm(Z2 - b * Zref) / torch.linalg.norm(Zref)).item())
+        assert dg.device_error() == 0
         # a directed graph: the transposed pass returns partial rows to owners
         drp, dcol, _ = G.rmat_gpu(15, 16 << 15, seed=10, device=dev, symmetric=False,
                                   loops=False)
@@ -70,24 +78,33 @@ def _worker(rank, world, port, q):
         a0, a1 = db[rank], db[rank + 1]
         ddg = DistGraph((drp[a0:a1 + 1] - drp[a0]).contiguous(),
                         dcol[drp[a0]:drp[a1]].contiguous(), db, rs_local=rsd[a0:a1].contiguous(),
-                        cs_global=None, tc_threshold=65)
+                        cs_global=None, tc_threshold=65, transport=transport)
         Zd = ddg.spmm_t(Gm[a0:a1].contiguous())
         dfull = tiles.from_csr(drp, dcol, ddeg.numel(), ddeg.numel(), kind="bcsc")
         Zdref = tiles.bcsc_spmm_t(dfull, Gm, tc_threshold=65, rs=rsd)[a0:a1]
         err = max(err, (torch.linalg.norm(Zd - Zdref) / torch.linalg.norm(Zdref)).item())
+        Yd = ddg.spmm(X[a0:a1].contiguous())
+        dfull_r = tiles.from_csr(drp, dcol, ddeg.numel(), ddeg.numel(), kind="bcsr")
+        Ydref = tiles.bcsr_spmm(dfull_r, X, tc_threshold=65, rs=rsd)[a0:a1]
+        err = max(err, (torch.linalg.norm(Yd - Ydref) / torch.linalg.norm(Ydref)).item())
         torch.cuda.synchronize()
+        assert ddg.device_error() == 0
+        dg.close()
+        ddg.close()
         q.put((rank, err, dg.halo_rows))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
-def test_row_partitioned_spmm_matches_single_gpu(gpu):
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_row_partitioned_spmm_matches_single_gpu(gpu, transport):
     world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, transport, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
