@@ -88,6 +88,9 @@ def parse():
                    help="exchange mode's halo transport: 'peer' = one kernel stores the rows "
                         "into the receivers' HBM over NVLink (CUDA IPC); 'nccl' = packed rows, "
                         "one NCCL all-to-all; 'auto' = peer when every GPU pair has peer access")
+    p.add_argument("--pair-reserve", default=None,
+                   help="exchange mode: four 0/1 digits, whether the local X, local G, halo X "
+                        "and halo G passes leave SMs free for the exchange (default: 1110)")
     p.add_argument("--workload", choices=["spmm", "gcn4", "config5"], default="spmm",
                    help="spmm: the config-2 SpMM step (headline); gcn4: config-4 GCN epoch time "
                         "(tcc_b200.train_gcn, epochs = --steps); config5: the scale-26 forward "
@@ -392,6 +395,8 @@ def run_ours(args, rank, world, local_rank):
         dg = DistGraph(lrp, lcol, bounds, rs_local=s[r0:r1].contiguous(), cs_global=s,
                        tc_threshold=thr, transport=args.transport)
         halo_rows = dg.halo_rows
+        if args.pair_reserve:
+            dg.pair_reserve = tuple(c == "1" for c in args.pair_reserve[:4])
         X_loc, G_loc = X_loc.contiguous(), G_loc.contiguous()
 
         def step(ev):
@@ -452,6 +457,13 @@ def run_ours(args, rank, world, local_rank):
                   ("pack0", "pack1", "xchg0", "xchg1", "local0", "done0", "local1", "done1")}
     mx = allreduce([ms, fwd_ms, bwd_ms] + ([phases[k] for k in sorted(phases)] if phases else []),
                    dist.ReduceOp.MAX if world > 1 else None, device)
+    by_rank = None
+    if phases and world > 1:  # every rank's phases (rows of an all-gather)
+        keys = sorted(phases)
+        mine = torch.tensor([phases[k] for k in keys], dtype=torch.float64, device=device)
+        allp = torch.empty((world, len(keys)), dtype=torch.float64, device=device)
+        dist.all_gather_into_tensor(allp, mine)
+        by_rank = [{k: round(v, 4) for k, v in zip(keys, row)} for row in allp.tolist()]
     ms, fwd_ms_max, bwd_ms_max = mx[:3]
     if mode == "exchange":  # the two passes interleave (local, local, halo, halo): half a step each
         fwd_ms = bwd_ms = ms / args.steps / 2
@@ -544,6 +556,8 @@ def run_ours(args, rank, world, local_rank):
                                     " each SpMM, overlapped with the local tiles"
                                     if mode == "exchange" else "X, G resident on every GPU")),
                    "transport": transport,
+                   "pair_reserve": ("".join("1" if x else "0" for x in dg.pair_reserve)
+                                    if mode == "exchange" else None),
                    "row_bounds": bounds if world > 1 else None,
                    "gen_s": round(gen_s, 3), "convert_s": round(conv_s, 3)},
         "parity": {"checker": "fp64 torch recomputation of sampled output rows (device gathers "
@@ -576,6 +590,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if phases:
         line["phases_ms_from_step_start"] = phases
+        if by_rank:
+            line["phases_ms_by_rank"] = by_rank
         line["phases_note"] = ("max over ranks of the mean over steps; pack/xchg: rows packed / "
                                "halo arrived (0 = X, 1 = G), local/done: local tiles / all tiles "
                                "of that SpMM finished")

@@ -313,7 +313,8 @@ typedef struct tcc_halo_push_args {
     uint64_t ldx, num_rows;
     const int64_t* send_idx; /* rows to send, grouped by receiver */
     uint32_t width, world, rank, tag, seq;
-    uint32_t max_blocks;     /* grid cap (0: 8 CTAs per SM) */
+    uint32_t max_blocks;     /* grid cap, CTAs of 512 threads (0: 4 per SM); one CTA per SM
+                                the concurrent kernels leave free is the intended use */
     uint64_t seg[TCC_PEER_MAX_RANKS + 1]; /* send_idx[seg[p]:seg[p+1]] go to rank p */
     float* dst[TCC_PEER_MAX_RANKS];       /* rank p's receive rows for this rank (mapped) */
     uint64_t ld_dst;                      /* their row stride (floats) */

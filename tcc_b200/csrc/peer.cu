@@ -10,7 +10,8 @@
 //        tag t (flags_g.freed[t][p] >= s-1), so the receive rows it is about
 //        to overwrite are no longer read;
 //     2. gathers its rows X[send_idx[i]] and stores them straight into the
-//        receivers' buffers over NVLink (a warp per row, 16-byte lanes): the
+//        receivers' buffers over NVLink (a warp moves 4 rows at a time in
+//        16-byte lanes, loads before stores): the
 //        pack and the transfer are one pass, no staging copy and no
 //        collective kernel;
 //     3. the last CTA to finish (a grid-wide counter) fences at system scope
@@ -94,7 +95,17 @@ struct PushParams {
     unsigned long long wait_ns;
 };
 
-__global__ void __launch_bounds__(256) halo_push_kernel(const __grid_constant__ PushParams a) {
+constexpr int kPushThreads = 512;
+constexpr int kPushRows = 4;  // rows a warp has in flight (loads before stores)
+
+// The segment (receiving rank) of send row i.
+__device__ __forceinline__ uint32_t segment_of(const PushParams& a, uint64_t i) {
+    uint32_t p = 0;
+    while (i >= a.seg[p + 1]) ++p;
+    return p;
+}
+
+__global__ void __launch_bounds__(kPushThreads) halo_push_kernel(const __grid_constant__ PushParams a) {
     __shared__ int ok;
     if (threadIdx.x == 0) {
         int good = 1;
@@ -113,21 +124,39 @@ __global__ void __launch_bounds__(256) halo_push_kernel(const __grid_constant__ 
     }
     __syncthreads();
     if (ok) {
+        // a warp moves kPushRows rows at a time: all their loads are issued
+        // before the first store, so each warp keeps kPushRows x 512 B of
+        // NVLink stores in flight (the stores are posted; nothing waits on them)
         const uint64_t n = a.seg[a.world];
         const int lane = threadIdx.x & 31;
         const uint64_t warps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
-        uint32_t p = 0;
-        for (uint64_t i = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n; i += warps) {
-            while (i >= a.seg[p + 1]) ++p;  // i only grows, so the segment only moves forward
-            const int64_t r = a.send_idx[i];
-            float4* dst = reinterpret_cast<float4*>(a.dst[p] + (i - a.seg[p]) * a.ld_dst);
-            if (r < 0 || (uint64_t)r >= a.num_rows) {  // a bad index: zero row, error recorded
-                if (lane == 0) atomicCAS(a.flags + kErrorWord, 0u, (uint32_t)TCC_DEVERR_INDEX_RANGE);
-                for (uint32_t c = lane; c < a.q4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                continue;
+        const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+        for (uint64_t base = gw * kPushRows; base < n; base += warps * kPushRows) {
+            const float4* src[kPushRows];
+            float4* dst[kPushRows];
+#pragma unroll
+            for (int u = 0; u < kPushRows; ++u) {
+                src[u] = nullptr;
+                dst[u] = nullptr;
+                const uint64_t i = base + u;
+                if (i >= n) continue;
+                const uint32_t p = segment_of(a, i);
+                dst[u] = reinterpret_cast<float4*>(a.dst[p] + (i - a.seg[p]) * a.ld_dst);
+                const int64_t r = a.send_idx[i];
+                if (r >= 0 && (uint64_t)r < a.num_rows)
+                    src[u] = reinterpret_cast<const float4*>(a.x + (uint64_t)r * a.ldx);
+                else if (lane == 0)  // a bad index: zero row, error recorded
+                    atomicCAS(a.flags + kErrorWord, 0u, (uint32_t)TCC_DEVERR_INDEX_RANGE);
             }
-            const float4* src = reinterpret_cast<const float4*>(a.x + (uint64_t)r * a.ldx);
-            for (uint32_t c = lane; c < a.q4; c += 32) dst[c] = __ldg(src + c);
+            for (uint32_t c = lane; c < a.q4; c += 32) {
+                float4 v[kPushRows];
+#pragma unroll
+                for (int u = 0; u < kPushRows; ++u)
+                    v[u] = src[u] ? __ldg(src[u] + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int u = 0; u < kPushRows; ++u)
+                    if (dst[u]) dst[u][c] = v[u];
+            }
         }
     }
     __syncthreads();
@@ -241,10 +270,11 @@ void halo_push(const tcc_halo_push_args* a, cudaStream_t s) {
     p.ld_dst = a->ld_dst;
     p.flags = static_cast<uint32_t*>(a->flags);
     p.wait_ns = a->wait_ns;
-    const uint64_t want = std::max<uint64_t>(1, (n + 7) / 8);
-    uint64_t cap = a->max_blocks ? a->max_blocks : (uint64_t)sm_count() * 8;
+    const uint64_t rows_per_block = (kPushThreads / 32) * kPushRows;
+    const uint64_t want = std::max<uint64_t>(1, (n + rows_per_block - 1) / rows_per_block);
+    const uint64_t cap = a->max_blocks ? a->max_blocks : (uint64_t)sm_count() * 4;
     const unsigned blocks = (unsigned)std::min<uint64_t>(want, cap);
-    halo_push_kernel<<<blocks, 256, 0, s>>>(p);
+    halo_push_kernel<<<blocks, kPushThreads, 0, s>>>(p);
     TCC_CUDA(cudaGetLastError());
 }
 

@@ -140,6 +140,9 @@ class DistGraph:
         self._side = None
         self._tstream = None
         self.comm_sms = 32  # SMs left to the exchange during the local tiles (measured best of 0-32)
+        # which passes of spmm_pair (local X, local G, halo X, halo G) leave
+        # comm_sms SMs free for the exchange still in flight
+        self.pair_reserve = (True, True, True, False)
         self.symmetric = symmetric
         self.tiles_loc = self.tiles_halo = None
         self.tiles_loc_t = self.tiles_halo_t = None  # BCSC tilings, built by the first spmm_t
@@ -154,6 +157,7 @@ class DistGraph:
             from .peer import PeerExchange, peers_reachable
             if peers_reachable(group):
                 self.peer = PeerExchange(group, self.send_idx, self.send_counts, self.recv_counts)
+                self.peer.max_blocks = self.comm_sms
             elif transport == "peer":
                 raise RuntimeError("transport='peer' needs peer access between every pair of GPUs")
         self.transport = "peer" if self.peer is not None else ("nccl" if self.world > 1 else "none")
@@ -310,16 +314,17 @@ class DistGraph:
             hx, wx = self.exchange(X_local, tag=0, timer=timer)
             hg, wg = self.exchange(G_local, tag=1, timer=timer)
         comm = wx is not None
-        self._local(X_local, Y, reserve=comm)
+        r = [comm and x for x in self.pair_reserve]
+        self._local(X_local, Y, reserve=r[0])
         if timer is not None:
             timer["local0"] = _event(main)
-        self._local(G_local, Z, reserve=comm)  # the halos are still on the wire
+        self._local(G_local, Z, reserve=r[1])  # the halos are still on the wire
         if timer is not None:
             timer["local1"] = _event(main)
-        self._halo(hx, wx, Y, reserve=comm)
+        self._halo(hx, wx, Y, reserve=r[2])
         if timer is not None:
             timer["done0"] = _event(main)
-        self._halo(hg, wg, Z)
+        self._halo(hg, wg, Z, reserve=r[3])
         if timer is not None:
             timer["done1"] = _event(main)
         return Y, Z

@@ -71,7 +71,9 @@ class PeerExchange:
         self.recv_counts = list(recv_counts)
         self.halo_rows = sum(self.recv_counts)
         self.wait_ns = int(wait_ns)
-        self.max_blocks = 64  # push CTAs (256 threads): enough to keep NVLink busy
+        # push CTAs (512 threads): DistGraph sets this to the SMs its pull
+        # kernels leave free, so the push never delays a pull CTA
+        self.max_blocks = 32
         self.seg = [0]
         for c in self.send_counts:
             self.seg.append(self.seg[-1] + c)
