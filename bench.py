@@ -88,6 +88,9 @@ def parse():
                    help="exchange mode's halo transport: 'peer' = one kernel stores the rows "
                         "into the receivers' HBM over NVLink (CUDA IPC); 'nccl' = packed rows, "
                         "one NCCL all-to-all; 'auto' = peer when every GPU pair has peer access")
+    p.add_argument("--peer-buffers", type=int, default=2,
+                   help="peer transport: receive buffers per tag a receiver rotates through "
+                        "(2: a sender may run a step ahead)")
     p.add_argument("--pair-reserve", default=None,
                    help="exchange mode: four 0/1 digits, whether the local X, local G, halo X "
                         "and halo G passes leave SMs free for the exchange (default: 1110)")
@@ -393,7 +396,7 @@ def run_ours(args, rank, world, local_rank):
     halo_rows = 0
     if mode == "exchange":
         dg = DistGraph(lrp, lcol, bounds, rs_local=s[r0:r1].contiguous(), cs_global=s,
-                       tc_threshold=thr, transport=args.transport)
+                       tc_threshold=thr, transport=args.transport, peer_buffers=args.peer_buffers)
         halo_rows = dg.halo_rows
         if args.pair_reserve:
             dg.pair_reserve = tuple(c == "1" for c in args.pair_reserve[:4])
@@ -558,6 +561,7 @@ def run_ours(args, rank, world, local_rank):
                    "transport": transport,
                    "pair_reserve": ("".join("1" if x else "0" for x in dg.pair_reserve)
                                     if mode == "exchange" else None),
+                   "peer_buffers": args.peer_buffers if transport == "peer" else None,
                    "row_bounds": bounds if world > 1 else None,
                    "gen_s": round(gen_s, 3), "convert_s": round(conv_s, 3)},
         "parity": {"checker": "fp64 torch recomputation of sampled output rows (device gathers "

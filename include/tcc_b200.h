@@ -282,7 +282,8 @@ tcc_status tcc_scatter_add_rows(const float* in, uint64_t ldi, const int64_t* id
  * with tcc_peer_alloc, the ranks swap the IPC handles (any host channel) and
  * map each other's with tcc_peer_open.  Per exchange (tag t, step number s,
  * counted the same on every rank, starting at 1):
- *   sender:   tcc_halo_push -- gathers its rows and stores them into the
+ *   sender:   tcc_halo_push -- once the receivers released the step that
+ *             last used the buffer, gathers its rows and stores them into the
  *             receivers' buffers over NVLink, then marks them arrived;
  *   receiver: tcc_halo_wait -- the stream continues once every sender's rows
  *             of step s arrived; the kernels after it read the buffer;
@@ -315,6 +316,9 @@ typedef struct tcc_halo_push_args {
     uint32_t width, world, rank, tag, seq;
     uint32_t max_blocks;     /* grid cap, CTAs of 512 threads (0: 4 per SM); one CTA per SM
                                 the concurrent kernels leave free is the intended use */
+    uint32_t buffers;        /* receive buffers each receiver rotates through for this tag
+                                (step s in buffer (s-1) % buffers; 0 means 1): the push
+                                waits for the receivers' release of step seq - buffers */
     uint64_t seg[TCC_PEER_MAX_RANKS + 1]; /* send_idx[seg[p]:seg[p+1]] go to rank p */
     float* dst[TCC_PEER_MAX_RANKS];       /* rank p's receive rows for this rank (mapped) */
     uint64_t ld_dst;                      /* their row stride (floats) */

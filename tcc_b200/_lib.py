@@ -64,7 +64,8 @@ class HaloPushArgs(C.Structure):
     _fields_ = [("x", C.c_void_p), ("ldx", C.c_uint64), ("num_rows", C.c_uint64),
                 ("send_idx", C.c_void_p), ("width", C.c_uint32), ("world", C.c_uint32),
                 ("rank", C.c_uint32), ("tag", C.c_uint32), ("seq", C.c_uint32),
-                ("max_blocks", C.c_uint32), ("seg", C.c_uint64 * (PEER_MAX_RANKS + 1)),
+                ("max_blocks", C.c_uint32), ("buffers", C.c_uint32),
+                ("seg", C.c_uint64 * (PEER_MAX_RANKS + 1)),
                 ("dst", C.c_void_p * PEER_MAX_RANKS), ("ld_dst", C.c_uint64),
                 ("peer_flags", C.c_void_p * PEER_MAX_RANKS), ("flags", C.c_void_p),
                 ("wait_ns", C.c_uint64)]

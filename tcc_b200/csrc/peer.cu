@@ -1,14 +1,15 @@
 // peer.cu -- the row-partitioned SpMM's halo exchange over NVLink peer memory.
 //
-// One process per GPU of one box.  Every rank owns, in its own HBM, one
-// receive buffer per exchange tag (the halo rows it reads, grouped by owner)
+// One process per GPU of one box.  Every rank owns, in its own HBM, one or
+// more receive buffers per exchange tag (the halo rows it reads, grouped by owner)
 // and one flag block; the peers map both through CUDA IPC.  One exchange of
 // tag t, step number s (the same count on every rank):
 //
 //   sender g (halo_push_kernel, on a side stream):
-//     1. waits until each receiver p it sends to has released step s-1 of
-//        tag t (flags_g.freed[t][p] >= s-1), so the receive rows it is about
-//        to overwrite are no longer read;
+//     1. waits until each receiver p it sends to has released step s-B of
+//        tag t (flags_g.freed[t][p] >= s-B, B the receive buffers a receiver
+//        rotates through, step s in buffer (s-1) % B), so the receive rows it
+//        is about to overwrite are no longer read;
 //     2. gathers its rows X[send_idx[i]] and stores them straight into the
 //        receivers' buffers over NVLink (a warp moves 4 rows at a time in
 //        16-byte lanes, loads before stores): the
@@ -86,7 +87,7 @@ struct PushParams {
     const float* x;
     uint64_t ldx, num_rows;
     const int64_t* send_idx;
-    uint32_t q4, world, rank, tag, seq;
+    uint32_t q4, world, rank, tag, seq, reuse;  // reuse: the step that last used the buffer
     uint64_t seg[kPeerMaxRanks + 1];
     float* dst[kPeerMaxRanks];
     uint64_t ld_dst;
@@ -109,10 +110,10 @@ __global__ void __launch_bounds__(kPushThreads) halo_push_kernel(const __grid_co
     __shared__ int ok;
     if (threadIdx.x == 0) {
         int good = 1;
-        if (a.seq > 1) {
+        if (a.reuse > 0) {
             for (uint32_t p = 0; p < a.world; ++p) {
                 if (a.seg[p + 1] == a.seg[p]) continue;
-                if (!wait_flag(a.flags + kFreedWord + a.tag * kPeerMaxRanks + p, a.seq - 1,
+                if (!wait_flag(a.flags + kFreedWord + a.tag * kPeerMaxRanks + p, a.reuse,
                                a.wait_ns)) {
                     record_timeout(a.flags);
                     good = 0;
@@ -267,6 +268,8 @@ void halo_push(const tcc_halo_push_args* a, cudaStream_t s) {
     p.rank = a->rank;
     p.tag = a->tag;
     p.seq = a->seq;
+    const uint32_t buffers = a->buffers ? a->buffers : 1;
+    p.reuse = a->seq > buffers ? a->seq - buffers : 0;
     p.ld_dst = a->ld_dst;
     p.flags = static_cast<uint32_t*>(a->flags);
     p.wait_ns = a->wait_ns;

@@ -89,7 +89,7 @@ class DistGraph:
 
     def __init__(self, rowptr: torch.Tensor, col: torch.Tensor, bounds: list, group=None,
                  rs_local=None, cs_global=None, tc_threshold: int = 12, build_tiles: bool = True,
-                 symmetric: bool = False, transport: str = "auto"):
+                 symmetric: bool = False, transport: str = "auto", peer_buffers: int = 2):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -156,7 +156,8 @@ class DistGraph:
         if self.world > 1 and rowptr.is_cuda and transport != "nccl":
             from .peer import PeerExchange, peers_reachable
             if peers_reachable(group):
-                self.peer = PeerExchange(group, self.send_idx, self.send_counts, self.recv_counts)
+                self.peer = PeerExchange(group, self.send_idx, self.send_counts, self.recv_counts,
+                                         buffers=peer_buffers)
                 self.peer.max_blocks = self.comm_sms
             elif transport == "peer":
                 raise RuntimeError("transport='peer' needs peer access between every pair of GPUs")
@@ -229,19 +230,23 @@ class DistGraph:
 
     def _peer_exchange(self, X_local, async_op, tag, timer):
         from .peer import PeerWork
-        recv = self.peer.recv_buffer(tag, X_local.shape[1])
         main = torch.cuda.current_stream(X_local.device)
         if self._side is None:
             self._side = torch.cuda.Stream(device=X_local.device, priority=-1)
         side = self._side
         side.wait_stream(main)
         seq = self.peer.push(X_local, tag, side)
+        recv = self.peer.recv_buffer(tag, X_local.shape[1], seq)
         if timer is not None:
             timer[f"pack{tag}"] = _event(side)  # this rank's rows stored at the receivers
         work = PeerWork(self.peer, tag, seq, X_local.device)
         if timer is not None:  # the arrival, seen from a stream nothing else waits on
             if self._tstream is None:
                 self._tstream = torch.cuda.Stream(device=X_local.device)
+            # the timing wait is a kernel: start it no earlier than this step,
+            # or it would sit on an SM through the previous step's passes (a
+            # pull CTA needs a whole SM's registers)
+            self._tstream.wait_stream(main)
             self.peer.wait(tag, seq, self._tstream)
             timer[f"xchg{tag}"] = _event(self._tstream)
         if not async_op:

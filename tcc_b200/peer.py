@@ -59,7 +59,7 @@ class PeerExchange:
     receiver; send_counts / recv_counts: rows to / from each rank (lists)."""
 
     def __init__(self, group, send_idx: torch.Tensor, send_counts: list, recv_counts: list,
-                 wait_ns: int = DEFAULT_WAIT_NS):
+                 wait_ns: int = DEFAULT_WAIT_NS, buffers: int = 2):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -71,6 +71,10 @@ class PeerExchange:
         self.recv_counts = list(recv_counts)
         self.halo_rows = sum(self.recv_counts)
         self.wait_ns = int(wait_ns)
+        # receive buffers per tag, step s in buffer (s - 1) % buffers: with two,
+        # a sender may run one step ahead of a receiver that is still reading
+        # the previous step's halo
+        self.buffers = max(1, int(buffers))
         # push CTAs (512 threads): DistGraph sets this to the SMs its pull
         # kernels leave free, so the push never delays a pull CTA
         self.max_blocks = 32
@@ -90,7 +94,7 @@ class PeerExchange:
         self._own = []     # allocations of this rank (freed by close)
         self._mapped = []  # peers' allocations mapped here (closed by close)
         self.flags, self.peer_flags = self._shared(L.PEER_FLAGS_BYTES)
-        self._bufs = {}    # (tag, width) -> (tensor view, [peer buffer base per rank])
+        self._bufs = {}    # (tag, width) -> [(tensor view, [peer buffer base per rank])] per buffer
         self.seq = [0] * L.PEER_MAX_TAGS
         self.closed = False
 
@@ -116,23 +120,28 @@ class PeerExchange:
             peers[p] = q.value
         return ptr.value, peers
 
-    def recv_buffer(self, tag: int, width: int) -> torch.Tensor:
-        """The halo buffer of ``tag`` at ``width`` floats per row (collective
-        on first use)."""
+    def _buffers(self, tag: int, width: int):
         key = (tag, width)
-        if key not in self._bufs:
+        if key not in self._bufs:  # collective on first use
             rows = max(self.halo_rows, 1)
-            own, peers = self._shared(rows * width * 4)
-            view = torch.as_tensor(_DeviceRows(own, rows, width), device=self.device)
-            self._bufs[key] = (view[:self.halo_rows], peers)
-        return self._bufs[key][0]
+            bufs = []
+            for _ in range(self.buffers):
+                own, peers = self._shared(rows * width * 4)
+                view = torch.as_tensor(_DeviceRows(own, rows, width), device=self.device)
+                bufs.append((view[:self.halo_rows], peers))
+            self._bufs[key] = bufs
+        return self._bufs[key]
+
+    def recv_buffer(self, tag: int, width: int, seq: int) -> torch.Tensor:
+        """The halo rows of step ``seq`` of ``tag`` at ``width`` floats per row."""
+        return self._buffers(tag, width)[(seq - 1) % self.buffers][0]
 
     def push(self, X: torch.Tensor, tag: int, stream: torch.cuda.Stream) -> int:
         """Send this rank's rows of X to their receivers (step number returned)."""
         width = X.shape[1]
-        self.recv_buffer(tag, width)
-        _, peers = self._bufs[(tag, width)]
+        bufs = self._buffers(tag, width)
         self.seq[tag] += 1
+        _, peers = bufs[(self.seq[tag] - 1) % self.buffers]
         a = L.HaloPushArgs()
         a.x = X.data_ptr()
         a.ldx = X.stride(0)
@@ -140,6 +149,7 @@ class PeerExchange:
         a.send_idx = self.send_idx.data_ptr() if self.send_idx.numel() else None
         a.width, a.world, a.rank, a.tag, a.seq = width, self.world, self.rank, tag, self.seq[tag]
         a.max_blocks = self.max_blocks
+        a.buffers = self.buffers
         for p in range(self.world + 1):
             a.seg[p] = self.seg[p]
         for p in range(self.world):

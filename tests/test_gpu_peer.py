@@ -27,12 +27,13 @@ def _error(flags):
     return code.value
 
 
-def _push(X, idx, dst, ld_dst, flags_send, flags_recv, seq, wait_ns, tag=0):
+def _push(X, idx, dst, ld_dst, flags_send, flags_recv, seq, wait_ns, tag=0, buffers=0):
     a = L.HaloPushArgs()
     a.x, a.ldx, a.num_rows = X.data_ptr(), X.stride(0), X.shape[0]
     a.send_idx = idx.data_ptr()
     a.width, a.world, a.rank, a.tag, a.seq = X.shape[1], 2, 0, tag, seq
     a.max_blocks = 0
+    a.buffers = buffers
     a.seg[0], a.seg[1], a.seg[2] = 0, 0, idx.numel()  # every row goes to rank 1
     a.dst[1] = dst
     a.ld_dst = ld_dst
@@ -88,6 +89,54 @@ def test_push_wait_release_and_timeout(gpu, width):
         assert torch.equal(X2[:4], X[:4] * 2 + 1)
     finally:
         del recv
+        for p in (buf, flags_s, flags_r):
+            L.call("tcc_peer_free", C.c_void_p(p))
+
+
+def test_two_receive_buffers(gpu):
+    """buffers = 2: step s goes to buffer (s-1) % 2, and a push waits only for
+    the release of step s-2, so steps 1 and 2 go out before any release."""
+    torch.cuda.synchronize()
+    width, n_local, n_send = 128, 2000, 1500
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    X = torch.randn((n_local, width), generator=gen, device="cuda")
+    idx = torch.randint(0, n_local, (n_send,), generator=gen, device="cuda", dtype=torch.int64)
+    flags_s, flags_r = _alloc(L.PEER_FLAGS_BYTES), _alloc(L.PEER_FLAGS_BYTES)
+    bufs = [_alloc(n_send * width * 4) for _ in range(2)]
+    views = [_as_tensor(b, n_send, width) for b in bufs]
+    release_to = (C.c_void_p * L.PEER_MAX_RANKS)(flags_s)
+    second = 1 << 30
+    try:
+        for s in (1, 2):  # no release in between
+            _push(X * s, idx, bufs[(s - 1) % 2], width, flags_s, flags_r, s, second, buffers=2)
+        L.call("tcc_halo_wait", C.c_void_p(flags_r), 0, 2, 0b01, second, None)
+        torch.cuda.synchronize()
+        assert _error(flags_s) == 0 and _error(flags_r) == 0
+        assert torch.equal(views[0], X[idx]) and torch.equal(views[1], 2 * X[idx])
+        # step 3 reuses buffer 0: it waits for step 1's release
+        _push(X * 3, idx, bufs[0], width, flags_s, flags_r, 3, 2_000_000, buffers=2)
+        torch.cuda.synchronize()
+        assert _error(flags_s) == L.DEVERR_WAIT_TIMEOUT
+        assert torch.equal(views[0], X[idx])
+    finally:
+        del views
+        for p in bufs + [flags_s, flags_r]:
+            L.call("tcc_peer_free", C.c_void_p(p))
+    # a fresh pair of flag blocks: release step 1, then step 3 goes out
+    flags_s, flags_r = _alloc(L.PEER_FLAGS_BYTES), _alloc(L.PEER_FLAGS_BYTES)
+    buf = _alloc(n_send * width * 4)
+    view = _as_tensor(buf, n_send, width)
+    release_to = (C.c_void_p * L.PEER_MAX_RANKS)(flags_s)
+    try:
+        _push(X, idx, buf, width, flags_s, flags_r, 1, second, buffers=2)
+        L.call("tcc_halo_release", release_to, 2, 1, 0, 1, 0b01, None)
+        _push(X * 3, idx, buf, width, flags_s, flags_r, 3, second, buffers=2)
+        L.call("tcc_halo_wait", C.c_void_p(flags_r), 0, 3, 0b01, second, None)
+        torch.cuda.synchronize()
+        assert _error(flags_s) == 0 and _error(flags_r) == 0
+        assert torch.equal(view, 3 * X[idx])
+    finally:
+        del view
         for p in (buf, flags_s, flags_r):
             L.call("tcc_peer_free", C.c_void_p(p))
 
