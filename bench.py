@@ -93,7 +93,8 @@ def parse():
                         "(2: a sender may run a step ahead)")
     p.add_argument("--pair-reserve", default=None,
                    help="exchange mode: four 0/1 digits, whether the local X, local G, halo X "
-                        "and halo G passes leave SMs free for the exchange (default: 1110)")
+                        "and halo G passes leave SMs free for the exchange (default: 1100 with "
+                        "the peer transport, 1110 with NCCL)")
     p.add_argument("--workload", choices=["spmm", "gcn4", "config5"], default="spmm",
                    help="spmm: the config-2 SpMM step (headline); gcn4: config-4 GCN epoch time "
                         "(tcc_b200.train_gcn, epochs = --steps); config5: the scale-26 forward "

@@ -141,7 +141,9 @@ class DistGraph:
         self._tstream = None
         self.comm_sms = 32  # SMs left to the exchange during the local tiles (measured best of 0-32)
         # which passes of spmm_pair (local X, local G, halo X, halo G) leave
-        # comm_sms SMs free for the exchange still in flight
+        # comm_sms SMs free for the exchange still in flight (set below by
+        # transport: the peer pushes end during the local passes, NCCL's
+        # all-to-all runs into the first halo pass)
         self.pair_reserve = (True, True, True, False)
         self.symmetric = symmetric
         self.tiles_loc = self.tiles_halo = None
@@ -162,6 +164,8 @@ class DistGraph:
             elif transport == "peer":
                 raise RuntimeError("transport='peer' needs peer access between every pair of GPUs")
         self.transport = "peer" if self.peer is not None else ("nccl" if self.world > 1 else "none")
+        if self.transport == "peer":
+            self.pair_reserve = (True, True, False, False)
         if build_tiles:
             from . import tiles
             self.tiles_loc = tiles.from_csr(self.loc_rowptr, self.loc_col, self.n_local,
