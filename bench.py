@@ -91,6 +91,9 @@ def parse():
     p.add_argument("--peer-buffers", type=int, default=2,
                    help="peer transport: receive buffers per tag a receiver rotates through "
                         "(2: a sender may run a step ahead)")
+    p.add_argument("--push-sms", type=int, default=0,
+                   help="peer transport: SMs for the halo push and held back from the local "
+                        "passes (0: sized per rank from its send rows and local tiles)")
     p.add_argument("--pair-reserve", default=None,
                    help="exchange mode: four 0/1 digits, whether the local X, local G, halo X "
                         "and halo G passes leave SMs free for the exchange (default: 1100 with "
@@ -395,12 +398,21 @@ def run_ours(args, rank, world, local_rank):
     Z = torch.empty((n_loc, F), device=device)
     X_loc, G_loc = X[r0:r1], Gm[r0:r1]
     halo_rows = 0
+    push_sms_all = None
     if mode == "exchange":
         dg = DistGraph(lrp, lcol, bounds, rs_local=s[r0:r1].contiguous(), cs_global=s,
                        tc_threshold=thr, transport=args.transport, peer_buffers=args.peer_buffers)
         halo_rows = dg.halo_rows
         if args.pair_reserve:
             dg.pair_reserve = tuple(c == "1" for c in args.pair_reserve[:4])
+        if args.push_sms and dg.peer is not None:
+            dg.comm_sms = dg.peer.max_blocks = args.push_sms
+        push_sms_all = [int(dg.comm_sms)]
+        if world > 1:  # every rank's exchange SMs (sized from its own rows and tiles)
+            t = torch.tensor([float(dg.comm_sms)], dtype=torch.float64, device=device)
+            g = torch.empty(world, dtype=torch.float64, device=device)
+            dist.all_gather_into_tensor(g, t)
+            push_sms_all = [int(v) for v in g.tolist()]
         X_loc, G_loc = X_loc.contiguous(), G_loc.contiguous()
 
         def step(ev):
@@ -563,6 +575,7 @@ def run_ours(args, rank, world, local_rank):
                    "pair_reserve": ("".join("1" if x else "0" for x in dg.pair_reserve)
                                     if mode == "exchange" else None),
                    "peer_buffers": args.peer_buffers if transport == "peer" else None,
+                   "exchange_sms_by_rank": push_sms_all if mode == "exchange" else None,
                    "row_bounds": bounds if world > 1 else None,
                    "gen_s": round(gen_s, 3), "convert_s": round(conv_s, 3)},
         "parity": {"checker": "fp64 torch recomputation of sampled output rows (device gathers "

@@ -70,6 +70,28 @@ def balanced_bounds(degrees: torch.Tensor, parts: int) -> list:
     return [0] + cuts + [int(degrees.numel())]
 
 
+# Rates behind push_sms, measured on B200 at F = 128 (both scale with F, so
+# their ratio holds at other widths): one 512-thread push CTA stores ~12 GB/s
+# of gathered rows over NVLink (210 MB in 0.47 ms on 32 CTAs), and one SM runs
+# ~12.3 K tiles per ms of the pull kernel (3.76 M tiles in 2.06 ms on 148).
+PUSH_BYTES_PER_CTA_MS = 12e6
+PULL_TILES_PER_SM_MS = 12.3e3
+
+
+def push_sms(send_rows: int, local_tiles: int, sms: int) -> int:
+    """SMs the peer push gets (and the local passes leave free) so that the
+    rank's pushes of a pipelined pair end about when its local passes do:
+    the push and local work split the SMs in proportion to their SM-time (at
+    F = 128; both scale with F).  A rank that sends little beside much local
+    work (2 GPUs: ~30 of 148) keeps most SMs for its tiles; one whose local
+    work shrank with N but whose halo did not (R-MAT at 4-8 GPUs) hands most
+    of them to the push."""
+    push = send_rows * 128 * 4 / PUSH_BYTES_PER_CTA_MS
+    local = local_tiles / PULL_TILES_PER_SM_MS
+    k = round(sms * push / max(push + local, 1e-9))
+    return int(max(16, min(sms - 16, k)))
+
+
 def _csr_from_pairs(rows: torch.Tensor, cols: torch.Tensor, n_rows: int):
     order = torch.argsort(rows * (1 << 32) + cols)
     rows, cols = rows[order], cols[order]
@@ -173,6 +195,10 @@ class DistGraph:
             if self.halo.numel():
                 self.tiles_halo = tiles.from_csr(self.halo_rowptr, self.halo_col, self.n_local,
                                                  int(self.halo.numel()), kind="bcsr")
+            if self.peer is not None:
+                sms = torch.cuda.get_device_properties(dev).multi_processor_count
+                self.comm_sms = push_sms(int(self.send_idx.numel()), self.tiles_loc.num_TCBlocks, sms)
+                self.peer.max_blocks = self.comm_sms
 
     def _exchange_counts(self, recv_counts):
         if self.world == 1:

@@ -114,3 +114,17 @@ def test_tile_balanced_bounds():
                 for k in range(parts)]
         # every part within one heavy window of the ideal share
         assert max(cost) <= sum(cost) / parts + 5000 + 50
+
+
+def test_push_sms_splits_the_sms_by_work():
+    """The peer push's SM share follows the ratio of its SM-time to the local
+    tiles' SM-time, within [16, sms - 16]."""
+    from tcc_b200.partition import push_sms
+    # 2 GPUs, config 2: heavy local work beside a modest send (~30 of 148)
+    assert 20 <= push_sms(410_000, 870_000, 148) <= 40
+    # little to send: the floor of 16
+    assert push_sms(1000, 1_000_000, 148) == 16
+    # a rank whose local work is small beside its send gets most SMs, never all
+    k = push_sms(500_000, 230_000, 148)
+    assert 70 <= k <= 132
+    assert push_sms(10_000_000, 1, 148) == 132
