@@ -76,6 +76,10 @@ def balanced_bounds(degrees: torch.Tensor, parts: int) -> list:
 # ~12.3 K tiles per ms of the pull kernel (3.76 M tiles in 2.06 ms on 148).
 PUSH_BYTES_PER_CTA_MS = 12e6
 PULL_TILES_PER_SM_MS = 12.3e3
+# Past ~64 CTAs a push gets no faster (4 GPUs, config 2: the largest sender's
+# push took 0.47 ms per operand on 64 CTAs and on 82), so more SMs would only
+# slow the rank's local passes.
+PUSH_SMS_CAP = 64
 
 
 def push_sms(send_rows: int, local_tiles: int, sms: int) -> int:
@@ -84,12 +88,12 @@ def push_sms(send_rows: int, local_tiles: int, sms: int) -> int:
     the push and local work split the SMs in proportion to their SM-time (at
     F = 128; both scale with F).  A rank that sends little beside much local
     work (2 GPUs: ~30 of 148) keeps most SMs for its tiles; one whose local
-    work shrank with N but whose halo did not (R-MAT at 4-8 GPUs) hands most
-    of them to the push."""
+    work shrank with N but whose halo did not (R-MAT at 4-8 GPUs) hands more
+    of them to the push, up to PUSH_SMS_CAP."""
     push = send_rows * 128 * 4 / PUSH_BYTES_PER_CTA_MS
     local = local_tiles / PULL_TILES_PER_SM_MS
     k = round(sms * push / max(push + local, 1e-9))
-    return int(max(16, min(sms - 16, k)))
+    return int(max(16, min(sms - 16, PUSH_SMS_CAP, k)))
 
 
 def _csr_from_pairs(rows: torch.Tensor, cols: torch.Tensor, n_rows: int):

@@ -124,7 +124,8 @@ def test_push_sms_splits_the_sms_by_work():
     assert 20 <= push_sms(410_000, 870_000, 148) <= 40
     # little to send: the floor of 16
     assert push_sms(1000, 1_000_000, 148) == 16
-    # a rank whose local work is small beside its send gets most SMs, never all
-    k = push_sms(500_000, 230_000, 148)
-    assert 70 <= k <= 132
-    assert push_sms(10_000_000, 1, 148) == 132
+    # a rank whose local work is small beside its send gets more SMs, up to the cap
+    assert 40 <= push_sms(300_000, 400_000, 148) < 64
+    assert push_sms(500_000, 230_000, 148) == 64
+    assert push_sms(10_000_000, 1, 148) == 64
+    assert push_sms(10_000_000, 1, 60) == 44  # and leaves 16 SMs to the tiles
