@@ -344,13 +344,16 @@ def time_steps(step, steps, warmup, world, local_rank, per_step_events=False):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    h0 = time.perf_counter()
     for i in range(steps):
         step(evs[i])
+    host_ms = (time.perf_counter() - h0) * 1e3
     e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
+    clocks["host_enqueue_ms"] = round(host_ms, 3)  # host time to enqueue the K steps
     return e0.elapsed_time(e1), evs, clocks
 
 
@@ -465,6 +468,8 @@ def run_ours(args, rank, world, local_rank):
                      dist.ReduceOp.MAX if world > 1 else None, device)
 
     ms, evs, clocks = time_steps(step, args.steps, args.warmup, world, local_rank)
+    host_ms = allreduce([clocks.pop("host_enqueue_ms") / args.steps],
+                        dist.ReduceOp.MAX if world > 1 else None, device)[0]
     fwd_ms = ev_ms(evs, "start", "done0")
     bwd_ms = ev_ms(evs, "done0", "done1")
     phases = None
@@ -604,6 +609,7 @@ def run_ours(args, rank, world, local_rank):
                 "api": "tcc_b200.hostio.HostPipeline (uploads, passes and downloads on three "
                        "streams; two device buffer sets alternate across steps)"},
         "gpu_launches": launches_per_step * args.steps,
+        "host_enqueue_ms_per_step": round(host_ms, 4),  # max over ranks; below ms_per_step: GPU-bound
         "clocks": clocks,
     }
     if phases:
