@@ -91,6 +91,9 @@ def parse():
     p.add_argument("--peer-buffers", type=int, default=2,
                    help="peer transport: receive buffers per tag a receiver rotates through "
                         "(2: a sender may run a step ahead)")
+    p.add_argument("--window-cost", type=float, default=2.0,
+                   help="N > 1: per-window cost (in tiles) added to each 8-row window's tile "
+                        "count when the rows are cut into equal-work parts")
     p.add_argument("--push-sms", type=int, default=0,
                    help="peer transport: SMs for the halo push and held back from the local "
                         "passes (0: sized per rank from its send rows and local tiles)")
@@ -392,7 +395,8 @@ def run_ours(args, rank, world, local_rank):
     gen_s = time.time() - t0
     t0 = time.time()
     full_bcsr = T.from_csr(rowptr, col, n, n, kind="bcsr")
-    bounds = [0, n] if world == 1 else tile_balanced_bounds(full_bcsr.windowOffset, n, world)
+    bounds = [0, n] if world == 1 else tile_balanced_bounds(full_bcsr.windowOffset, n, world,
+                                                            window_cost=args.window_cost)
     r0, r1 = bounds[rank], bounds[rank + 1]
     n_loc = r1 - r0
     lrp, lcol = row_block(rowptr, col, r0, r1)
@@ -582,6 +586,7 @@ def run_ours(args, rank, world, local_rank):
                    "peer_buffers": args.peer_buffers if transport == "peer" else None,
                    "exchange_sms_by_rank": push_sms_all if mode == "exchange" else None,
                    "row_bounds": bounds if world > 1 else None,
+                   "window_cost": args.window_cost if world > 1 else None,
                    "gen_s": round(gen_s, 3), "convert_s": round(conv_s, 3)},
         "parity": {"checker": "fp64 torch recomputation of sampled output rows (device gathers "
                               "+ index_add), before timing",
