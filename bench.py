@@ -91,9 +91,10 @@ def parse():
     p.add_argument("--peer-buffers", type=int, default=2,
                    help="peer transport: receive buffers per tag a receiver rotates through "
                         "(2: a sender may run a step ahead)")
-    p.add_argument("--window-cost", type=float, default=2.0,
+    p.add_argument("--window-cost", type=float, default=None,
                    help="N > 1: per-window cost (in tiles) added to each 8-row window's tile "
-                        "count when the rows are cut into equal-work parts")
+                        "count when the rows are cut into equal-work parts (default: 2 in "
+                        "replicated mode; partition.exchange_window_cost(N) in exchange mode)")
     p.add_argument("--push-sms", type=int, default=0,
                    help="peer transport: SMs for the halo push and held back from the local "
                         "passes (0: sized per rank from its send rows and local tiles)")
@@ -381,7 +382,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     from tcc_b200 import tiles as T
     from tcc_b200.hostio import HostPipeline
-    from tcc_b200.partition import DistGraph, tile_balanced_bounds
+    from tcc_b200.partition import DistGraph, exchange_window_cost, tile_balanced_bounds
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     mode = "single" if world == 1 else args.dist_mode
@@ -395,6 +396,8 @@ def run_ours(args, rank, world, local_rank):
     gen_s = time.time() - t0
     t0 = time.time()
     full_bcsr = T.from_csr(rowptr, col, n, n, kind="bcsr")
+    if args.window_cost is None:
+        args.window_cost = exchange_window_cost(world) if mode == "exchange" else 2.0
     bounds = [0, n] if world == 1 else tile_balanced_bounds(full_bcsr.windowOffset, n, world,
                                                             window_cost=args.window_cost)
     r0, r1 = bounds[rank], bounds[rank + 1]

@@ -417,6 +417,17 @@ class DistGraph:
         return Z
 
 
+def exchange_window_cost(parts: int) -> float:
+    """Per-window cost for tile_balanced_bounds when the halo is exchanged
+    every pass.  On 2 GPUs a rank's local tiles outweigh the rows it sends,
+    and balancing tiles is best (config 2: 2.90 ms per step at 2 against 3.00
+    at 6).  From 4 GPUs on, the rank that sends the most rows (the power-law
+    tail, whose rows many windows reference) paces every rank's halo passes,
+    so each window also carries its rows' share of the sending (config 2 at
+    4 GPUs: 2.05 / 1.98 / 1.90 ms per step at 2 / 6 / 10)."""
+    return 2.0 if parts <= 2 else 10.0
+
+
 def tile_balanced_bounds(window_offset: torch.Tensor, num_rows: int, parts: int,
                          window_cost: float = 2.0) -> list:
     """Contiguous row bounds, on window boundaries (multiples of 8), with about

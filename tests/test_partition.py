@@ -129,3 +129,22 @@ def test_push_sms_splits_the_sms_by_work():
     assert push_sms(500_000, 230_000, 148) == 64
     assert push_sms(10_000_000, 1, 148) == 64
     assert push_sms(10_000_000, 1, 60) == 44  # and leaves 16 SMs to the tiles
+
+
+def test_exchange_window_cost_by_rank_count():
+    """Tiles alone on 2 ranks, tiles plus the rows' sending from 4 on; a larger
+    per-window cost moves rows off the tail part."""
+    import torch
+    from tcc_b200.partition import exchange_window_cost, tile_balanced_bounds
+    assert exchange_window_cost(2) == 2.0 and exchange_window_cost(4) == 10.0
+    assert exchange_window_cost(8) == 10.0
+    # hub windows hold many tiles, tail windows one: the tail part shrinks as
+    # the per-window cost grows
+    tiles = torch.tensor([40] * 100 + [1] * 3900, dtype=torch.int64)
+    off = torch.zeros(tiles.numel() + 1, dtype=torch.int64)
+    off[1:] = torch.cumsum(tiles, 0)
+    n = 8 * tiles.numel()
+    b2 = tile_balanced_bounds(off, n, 4, window_cost=2.0)
+    b10 = tile_balanced_bounds(off, n, 4, window_cost=10.0)
+    assert b2[0] == 0 and b2[-1] == n and b10[-1] == n
+    assert n - b10[3] < n - b2[3]
