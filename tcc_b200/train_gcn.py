@@ -52,7 +52,7 @@ from . import graphs as G
 from . import tiles as T
 from .feature_store import FeatureStore
 from .gcn import relu_dropout
-from .partition import DistGraph, balanced_bounds, nccl_options
+from .partition import DistGraph, balanced_bounds, nccl_options, tile_balanced_bounds
 
 
 def _store_aggregate(tiles_g: T.Tiles, store: FeatureStore, rs: torch.Tensor,
@@ -99,7 +99,14 @@ def build(cfg: dict, device, world: int, rank: int):
     t0 = time.time()
     rowptr, col, _ = G.rmat_gpu(scale, edges, seed=seed, device=device, n=n)
     deg = torch.diff(rowptr)
-    bounds = balanced_bounds(deg, world)
+    if world > 1 and cfg.get("partition", "tiles") == "tiles":
+        # equal pull work per rank: R-MAT's hub rows pack many nonzeros into
+        # few tiles, so equal nonzeros leave the tail ranks slower
+        full = T.from_csr(rowptr, col, n, n, kind="bcsr")
+        bounds = tile_balanced_bounds(full.windowOffset, n, world)
+        del full
+    else:
+        bounds = balanced_bounds(deg, world)
     r0, r1 = bounds[rank], bounds[rank + 1]
     s = deg.to(torch.float64).clamp(min=1).rsqrt().to(torch.float32)  # D^-1/2 of A + I
     lrp = (rowptr[r0:r1 + 1] - rowptr[r0]).contiguous()
@@ -286,6 +293,9 @@ def main(argv=None):
                        help="layer 2 as (A.H).W, the reference's order")
     p.add_argument("--cold-zero-copy", action="store_true",
                    help="read cold rows from pinned host memory in every gather (no HBM staging)")
+    p.add_argument("--partition", choices=["tiles", "nnz"], default="tiles",
+                   help="N > 1: cut the rows into parts of equal pull work (tiles) or equal "
+                        "nonzeros")
     p.add_argument("--save", default=None, help="checkpoint path written at the end (rank 0)")
     p.add_argument("--resume", default=None, help="checkpoint to continue from")
     a = p.parse_args(argv)
@@ -302,6 +312,7 @@ def main(argv=None):
         cfg["epochs"] = a.epochs
         cfg["save"], cfg["resume"] = a.save, a.resume
         cfg["cold_staging"] = not a.cold_zero_copy
+        cfg["partition"] = a.partition
         tf = {"transform": True, "aggregate": False}.get(a.order)
         r = train(cfg, device, world, rank, tf)
         if rank == 0:
@@ -321,6 +332,7 @@ def main(argv=None):
                                               if r["cold_staging"]
                                               else "zero-copy reads of pinned host memory"),
                            "halo_transport": r["transport"],
+                           "partition": cfg["partition"] if world > 1 else None,
                            "halo_rows_total": int(r["halo_rows"]), "transform_first": r["transform_first"],
                            "order": "layer 1 from the hot/cold store, layer 2 over the row partition"}}),
                   flush=True)
