@@ -19,8 +19,12 @@ __device__ __forceinline__ float comp(const float4& v, int c) {
 // pass2 == false: one TF32 pass with operands rounded like cvt.rna (the
 // reference's dense-tile arithmetic).  pass2 == true: fp32-accurate split
 // x = hi + lo (hi = x with the low 13 bits cleared, exact), all hi MMAs
-// first, then all lo MMAs.  The hi MMAs take the raw fp32 bits: the tensor
-// core ignores the low 13 bits of a TF32 operand, which leaves exactly hi.
+// first, then all lo MMAs.  The hi MMAs take the raw fp32 bits and rely on
+// the tensor core reading only the TF32 bits of an operand (the low 13 bits
+// dropped, which leaves exactly hi).  That is behaviour measured on B200, not
+// a documented guarantee: the fp32-accuracy tests (1e-5 relative against fp64
+// CSR products, every tile on this path) check it, and masking hi explicitly
+// would cost one AND per operand.
 template <int NP>
 __device__ __forceinline__ void tile_mma(float (&dacc)[4 * NP][4], const float4 (&x)[2][2 * NP],
                                          uint64_t bm, int gid, int tig, bool pass2) {
