@@ -335,7 +335,15 @@ class DistGraph:
             halo, work = self.exchange(X_local)
         Y = self._local(X_local, out, reserve=work is not None)
         self._halo(halo, work, Y)
+        self._join_side(X_local.device)
         return Y
+
+    def _join_side(self, device):
+        """The caller's stream waits for the side stream's push (which reads
+        the caller's rows), so the caller may overwrite or free them after
+        the call; the push has long finished by then, so this costs nothing."""
+        if self._side is not None:
+            torch.cuda.current_stream(device).wait_stream(self._side)
 
     def spmm_pair(self, X_local: torch.Tensor, Y: torch.Tensor, G_local: torch.Tensor,
                   Z: torch.Tensor, timer: dict | None = None):
@@ -366,6 +374,7 @@ class DistGraph:
         self._halo(hg, wg, Z, reserve=r[3])
         if timer is not None:
             timer["done1"] = _event(main)
+        self._join_side(X_local.device)
         return Y, Z
 
     def spmm_t(self, G_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
