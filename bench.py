@@ -95,6 +95,9 @@ def parse():
                    help="N > 1: per-window cost (in tiles) added to each 8-row window's tile "
                         "count when the rows are cut into equal-work parts (default: 2 in "
                         "replicated mode; partition.exchange_window_cost(N) in exchange mode)")
+    p.add_argument("--host-step", choices=["native", "python"], default="native",
+                   help="peer transport: a step sequenced by one tcc_dist_step call (native) "
+                        "or call by call from Python")
     p.add_argument("--push-sms", type=int, default=0,
                    help="peer transport: SMs for the halo push and held back from the local "
                         "passes (0: sized per rank from its send rows and local tiles)")
@@ -415,6 +418,7 @@ def run_ours(args, rank, world, local_rank):
         halo_rows = dg.halo_rows
         if args.pair_reserve:
             dg.pair_reserve = tuple(c == "1" for c in args.pair_reserve[:4])
+        dg.host_step = args.host_step
         if args.push_sms and dg.peer is not None:
             dg.comm_sms = dg.peer.max_blocks = args.push_sms
         push_sms_all = [int(dg.comm_sms)]
@@ -588,6 +592,8 @@ def run_ours(args, rank, world, local_rank):
                                     if mode == "exchange" else None),
                    "peer_buffers": args.peer_buffers if transport == "peer" else None,
                    "exchange_sms_by_rank": push_sms_all if mode == "exchange" else None,
+                   "host_step": (args.host_step if mode == "exchange" and transport == "peer"
+                                 else None),
                    "row_bounds": bounds if world > 1 else None,
                    "window_cost": args.window_cost if world > 1 else None,
                    "gen_s": round(gen_s, 3), "convert_s": round(conv_s, 3)},

@@ -337,6 +337,49 @@ tcc_status tcc_halo_release(void* const* peer_flags, uint32_t world, uint32_t ra
 /* The flag block's device error word (TCC_DEVERR_*; synchronises `stream`). */
 tcc_status tcc_peer_device_error(void* flags, int* code, cudaStream_t stream);
 
+/* One step of the row-partitioned SpMM on this rank, enqueued by the library:
+ * for each operand (one, or two pipelined -- a training step's forward and
+ * backward), push the rows the peers need (on `side`), then on `main` the
+ * local-column tiles of every operand, then per operand the arrival wait, the
+ * halo-column tiles (accumulated) and the release.  Y = diag(rs) A_loc
+ * diag(cs_local) X + diag(rs) A_halo diag(cs_halo) X_halo.  `side` first waits
+ * for `main`, and `main` ends waiting for `side` (the pushes read X).  No
+ * reference counterpart (the reference's kernels load peer caches in place,
+ * cnic/src/core/spmm_kernel.cu:145-147); this is the C++ form of
+ * tcc_b200.partition.DistGraph.spmm_pair with the peer transport. */
+typedef struct tcc_dist_operand {
+    tcc_halo_push_args push; /* push.x = this rank's rows of the operand; push.seq = the step */
+    const float* halo;       /* this rank's receive rows of step push.seq (its own buffer) */
+    uint64_t ld_halo;
+    float* y;                /* output rows [local rows x push.width] */
+    uint64_t ldy;
+} tcc_dist_operand;
+
+typedef struct tcc_dist_step_args {
+    const tcc_bcsr* local;   /* local-column tiles (columns remapped to this rank's rows) */
+    void* local_scratch;     /* their pull scratch (tcc_pull_scratch_bytes) */
+    size_t local_scratch_bytes;
+    int32_t local_plan_ready;
+    const tcc_bcsr* halo;    /* halo-column tiles, NULL when the rank has no halo */
+    void* halo_scratch;
+    size_t halo_scratch_bytes;
+    int32_t halo_plan_ready;
+    const float* rs;         /* row scale of the local rows, or NULL */
+    const float* cs_local;   /* column scale of the local columns, or NULL */
+    const float* cs_halo;    /* column scale of the halo columns, or NULL */
+    uint32_t tc_threshold;
+    uint32_t recv_mask;      /* bit p: rank p sends rows to this rank */
+    uint32_t reserve_sms;    /* SMs left to the pushes during the passes in reserve_passes */
+    uint32_t reserve_passes; /* bit 0/1: local pass of operand 0/1; bit 2/3: halo pass */
+    void* peer_flags[TCC_PEER_MAX_RANKS]; /* rank p's mapped flag block (for the release) */
+    uint32_t n_ops;          /* 1 or 2 */
+    tcc_dist_operand ops[2];
+    cudaEvent_t events[6];   /* optional, NULL to skip: [0,1] pushes done (side), [2,3]
+                                local passes done, [4,5] operands done (main) */
+} tcc_dist_step_args;
+
+tcc_status tcc_dist_step(const tcc_dist_step_args* args, cudaStream_t main, cudaStream_t side);
+
 /* tf32_spmm_bcsr + tf32_computeX128TransposePipe2_BCSR
  * (cnic/src/core/spmm_dispatcher.cu:166-233, spmm_kernel.cu:1560-1843):
  * C[num_rows x F] = diag(rs) * A * diag(cs) * B[num_cols x F]; row windows own

@@ -71,6 +71,25 @@ class HaloPushArgs(C.Structure):
                 ("wait_ns", C.c_uint64)]
 
 
+class DistOperand(C.Structure):
+    """tcc_dist_operand."""
+    _fields_ = [("push", HaloPushArgs), ("halo", C.c_void_p), ("ld_halo", C.c_uint64),
+                ("y", C.c_void_p), ("ldy", C.c_uint64)]
+
+
+class DistStepArgs(C.Structure):
+    """tcc_dist_step_args."""
+    _fields_ = [("local", C.c_void_p), ("local_scratch", C.c_void_p),
+                ("local_scratch_bytes", C.c_size_t), ("local_plan_ready", C.c_int32),
+                ("halo", C.c_void_p), ("halo_scratch", C.c_void_p),
+                ("halo_scratch_bytes", C.c_size_t), ("halo_plan_ready", C.c_int32),
+                ("rs", C.c_void_p), ("cs_local", C.c_void_p), ("cs_halo", C.c_void_p),
+                ("tc_threshold", C.c_uint32), ("recv_mask", C.c_uint32),
+                ("reserve_sms", C.c_uint32), ("reserve_passes", C.c_uint32),
+                ("peer_flags", C.c_void_p * PEER_MAX_RANKS), ("n_ops", C.c_uint32),
+                ("ops", DistOperand * 2), ("events", C.c_void_p * 6)]
+
+
 class Bcsr(C.Structure):
     """Field-for-field tcc_bcsr / the reference's BCSR<float>."""
     _fields_ = [("num_rows", C.c_uint32), ("num_cols", C.c_uint32), ("nnz", C.c_uint32),
@@ -137,6 +156,7 @@ PROTOTYPES = {
     "tcc_halo_wait": (_st, [_vp, _u32, _u32, _u32, _u64, _vp]),
     "tcc_halo_release": (_st, [C.POINTER(_vp), _u32, _u32, _u32, _u32, _u32, _vp]),
     "tcc_peer_device_error": (_st, [_vp, C.POINTER(_i), _vp]),
+    "tcc_dist_step": (_st, [C.POINTER(DistStepArgs), _vp, _vp]),
     "tcc_relu_dropout_forward": (_st, [_vp, _vp, _u64, C.c_float, _u64, _vp]),
     "tcc_relu_dropout_backward": (_st, [_vp, _vp, _vp, _u64, C.c_float, _vp]),
     "tcc_bcsr_spmm_t": (_st, [C.POINTER(Bcsr), _vp, _u64, _vp, _u64, _u32, _u32, _vp, _vp, _vp]),

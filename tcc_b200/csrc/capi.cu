@@ -552,6 +552,92 @@ tcc_status tcc_peer_device_error(void* flags, int* code, cudaStream_t stream) {
     return guarded("tcc_peer_device_error", [&] { tcc::peer_device_error(flags, code, stream); });
 }
 
+namespace {
+
+// Fork/join events of tcc_dist_step, one pair per host thread and device.
+struct StepEvents {
+    int device = -1;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+thread_local StepEvents g_step_events;
+
+StepEvents& step_events() {
+    int dev = 0;
+    TCC_CUDA(cudaGetDevice(&dev));
+    StepEvents& e = g_step_events;
+    if (e.device != dev) {
+        TCC_CUDA(cudaEventCreateWithFlags(&e.fork, cudaEventDisableTiming));
+        TCC_CUDA(cudaEventCreateWithFlags(&e.join, cudaEventDisableTiming));
+        e.device = dev;
+    }
+    return e;
+}
+
+// The pull kernels' SM reserve for the scope of one pass.
+struct ReserveScope {
+    uint32_t prev;
+    explicit ReserveScope(uint32_t sms) : prev(tcc::grid_reserve()) { tcc::set_grid_reserve(sms); }
+    ~ReserveScope() { tcc::set_grid_reserve(prev); }
+};
+
+}  // namespace
+
+tcc_status tcc_dist_step(const tcc_dist_step_args* a, cudaStream_t main, cudaStream_t side) {
+    return guarded("tcc_dist_step", [&] {
+        TCC_REQUIRE(a, "args must not be NULL");
+        TCC_REQUIRE(a->n_ops == 1 || a->n_ops == 2, "n_ops must be 1 or 2");
+        check_bcsr(a->local);
+        if (a->halo) check_bcsr(a->halo);
+        for (uint32_t i = 0; i < a->n_ops; ++i) {
+            const tcc_dist_operand& op = a->ops[i];
+            TCC_REQUIRE(op.push.x && op.y, "operand rows and outputs must not be NULL");
+            TCC_REQUIRE(op.push.num_rows == a->local->num_rows && a->local->num_cols == a->local->num_rows,
+                        "the local tiles cover this rank's rows and columns");
+            TCC_REQUIRE(!a->halo || op.halo || a->halo->num_TCBlocks == 0,
+                        "halo rows must not be NULL when there are halo tiles");
+        }
+        auto record = [&](int k, cudaStream_t s) {
+            if (a->events[k]) TCC_CUDA(cudaEventRecord(a->events[k], s));
+        };
+        StepEvents& ev = step_events();
+        TCC_CUDA(cudaEventRecord(ev.fork, main));
+        TCC_CUDA(cudaStreamWaitEvent(side, ev.fork, 0));
+        for (uint32_t i = 0; i < a->n_ops; ++i) {
+            tcc::halo_push(&a->ops[i].push, side);
+            record((int)i, side);
+        }
+        const tcc::PullTiles loc = bcsr_pull(a->local);
+        bool loc_ready = a->local_plan_ready != 0;
+        for (uint32_t i = 0; i < a->n_ops; ++i) {
+            const tcc_dist_operand& op = a->ops[i];
+            ReserveScope r((a->reserve_passes >> i & 1u) ? a->reserve_sms : 0);
+            tcc::Dense d{op.push.x, op.push.ldx, op.y, op.ldy, op.push.width, a->rs, a->cs_local};
+            tcc::pull_spmm(loc, d, a->tc_threshold, 0, a->local_scratch, a->local_scratch_bytes,
+                           loc_ready, nullptr, main);
+            loc_ready = true;
+            record(2 + (int)i, main);
+        }
+        bool halo_ready = a->halo_plan_ready != 0;
+        for (uint32_t i = 0; i < a->n_ops; ++i) {
+            const tcc_dist_operand& op = a->ops[i];
+            tcc::halo_wait(op.push.flags, op.push.tag, op.push.seq, a->recv_mask, op.push.wait_ns,
+                           main);
+            if (a->halo && a->halo->num_TCBlocks) {
+                ReserveScope r((a->reserve_passes >> (2 + i) & 1u) ? a->reserve_sms : 0);
+                tcc::Dense d{op.halo, op.ld_halo, op.y, op.ldy, op.push.width, a->rs, a->cs_halo};
+                tcc::pull_spmm(bcsr_pull(a->halo), d, a->tc_threshold, 1, a->halo_scratch,
+                               a->halo_scratch_bytes, halo_ready, nullptr, main);
+                halo_ready = true;
+            }
+            tcc::halo_release(a->peer_flags, op.push.world, op.push.rank, op.push.tag, op.push.seq,
+                              a->recv_mask, main);
+            record(4 + (int)i, main);
+        }
+        TCC_CUDA(cudaEventRecord(ev.join, side));
+        TCC_CUDA(cudaStreamWaitEvent(main, ev.join, 0));
+    });
+}
+
 tcc_status tcc_relu_dropout_forward(const float* in, float* out, uint64_t n, float p,
                                     uint64_t seed, cudaStream_t stream) {
     return guarded("tcc_relu_dropout_forward", [&] {

@@ -171,6 +171,10 @@ class DistGraph:
         # transport: the peer pushes end during the local passes, NCCL's
         # all-to-all runs into the first halo pass)
         self.pair_reserve = (True, True, True, False)
+        # who sequences a step with the peer transport: "native" -- one call
+        # of tcc_dist_step, the library enqueues the pushes, passes, waits and
+        # releases; "python" -- the same sequence from here, call by call
+        self.host_step = "native"
         self.symmetric = symmetric
         self.tiles_loc = self.tiles_halo = None
         self.tiles_loc_t = self.tiles_halo_t = None  # BCSC tilings, built by the first spmm_t
@@ -331,12 +335,90 @@ class DistGraph:
         """Y[P_g] = (diag(rs) A diag(cs) X)[P_g], exchange overlapped with the
         local-column tiles."""
         X_local = X_local.contiguous()
+        if self._native():
+            if out is None:
+                out = torch.empty((self.n_local, X_local.shape[1]), dtype=X_local.dtype,
+                                  device=X_local.device)
+            self._native_step([(X_local, out, 0)], (True, False, False, False))
+            return out
         with torch.cuda.nvtx.range("tcc.halo_exchange_start"):
             halo, work = self.exchange(X_local)
         Y = self._local(X_local, out, reserve=work is not None)
         self._halo(halo, work, Y)
         self._join_side(X_local.device)
         return Y
+
+    def _native(self) -> bool:
+        return self.host_step == "native" and self.peer is not None and self.tiles_loc is not None
+
+    def _native_step(self, ops, reserve, timer=None):
+        """One step enqueued by the library (tcc_dist_step): ops = [(X_local,
+        Y, tag)] for one or two operands; reserve = which of the passes (local
+        0, local 1, halo 0, halo 1) leave comm_sms SMs to the pushes."""
+        import ctypes as C
+        from . import _lib as L
+        dev = ops[0][0].device
+        main = torch.cuda.current_stream(dev)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=dev, priority=-1)
+        a = L.DistStepArgs()
+        keep = []  # ctypes structs the call reads
+        sl = self.tiles_loc.struct()
+        keep.append(sl)
+        a.local = C.addressof(sl)
+        sc = self.tiles_loc.scratch()
+        a.local_scratch, a.local_scratch_bytes = sc.data_ptr(), sc.numel()
+        a.local_plan_ready = int(self.tiles_loc._plan_ready)
+        if self.tiles_halo is not None:
+            sh = self.tiles_halo.struct()
+            keep.append(sh)
+            a.halo = C.addressof(sh)
+            hc = self.tiles_halo.scratch()
+            a.halo_scratch, a.halo_scratch_bytes = hc.data_ptr(), hc.numel()
+            a.halo_plan_ready = int(self.tiles_halo._plan_ready)
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        a.rs, a.cs_local, a.cs_halo = ptr(self.rs), ptr(self.cs_local), ptr(self.cs_halo)
+        a.tc_threshold = self.tc_threshold
+        a.recv_mask = self.peer.recv_mask
+        a.reserve_sms = self.comm_sms
+        a.reserve_passes = sum(1 << i for i, x in enumerate(reserve) if x)
+        for p in range(self.world):
+            a.peer_flags[p] = self.peer.peer_flags[p] or 0
+        a.n_ops = len(ops)
+        if timer is not None:
+            timer["start"] = _event(main)
+        seqs = []
+        for i, (X, Y, tag) in enumerate(ops):
+            pa = self.peer.push_args(X, tag)
+            seqs.append((tag, pa.seq))
+            op = a.ops[i]
+            op.push = pa
+            halo = self.peer.recv_buffer(tag, X.shape[1], pa.seq)
+            op.halo, op.ld_halo = (halo.data_ptr() if halo.numel() else None), X.shape[1]
+            op.y, op.ldy = Y.data_ptr(), Y.stride(0)
+        if timer is not None:
+            names = [f"pack{i}" for i in range(len(ops))] + [f"local{i}" for i in range(len(ops))] + \
+                    [f"done{i}" for i in range(len(ops))]
+            slots = list(range(len(ops))) + [2 + i for i in range(len(ops))] + \
+                [4 + i for i in range(len(ops))]
+            for name, k in zip(names, slots):
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(main)  # creates the event; the library records it again in place
+                timer[name] = e
+                a.events[k] = e.cuda_event
+            if self._tstream is None:
+                self._tstream = torch.cuda.Stream(device=dev)
+            self._tstream.wait_stream(main)
+            for i, (tag, seq) in enumerate(seqs):  # arrival, seen from a stream nothing waits on
+                self.peer.wait(tag, seq, self._tstream)
+                timer[f"xchg{i}"] = _event(self._tstream)
+        with torch.cuda.nvtx.range("tcc.dist_step"):
+            L.call("tcc_dist_step", C.byref(a), C.c_void_p(main.cuda_stream),
+                   C.c_void_p(self._side.cuda_stream))
+        self.tiles_loc._plan_ready = True
+        if self.tiles_halo is not None:
+            self.tiles_halo._plan_ready = True
+        del keep
 
     def _join_side(self, device):
         """The caller's stream waits for the side stream's push (which reads
@@ -354,6 +436,9 @@ class DistGraph:
         that receives CUDA events -- "start", "pack0/1", "xchg0/1" (halos
         arrived), "local0/1" (local tiles of Y / Z done) and "done0/1" (Y, Z
         complete)."""
+        if self._native():
+            self._native_step([(X_local, Y, 0), (G_local, Z, 1)], self.pair_reserve, timer)
+            return Y, Z
         main = torch.cuda.current_stream(X_local.device)
         if timer is not None:
             timer["start"] = _event(main)

@@ -138,6 +138,14 @@ class PeerExchange:
 
     def push(self, X: torch.Tensor, tag: int, stream: torch.cuda.Stream) -> int:
         """Send this rank's rows of X to their receivers (step number returned)."""
+        a = self.push_args(X, tag)
+        L.call("tcc_halo_push", C.byref(a), C.c_void_p(stream.cuda_stream))
+        return a.seq
+
+    def push_args(self, X: torch.Tensor, tag: int) -> "L.HaloPushArgs":
+        """tcc_halo_push's arguments for the next step of ``tag`` (the step
+        number advances; the caller launches the push, e.g. through
+        tcc_dist_step)."""
         width = X.shape[1]
         bufs = self._buffers(tag, width)
         self.seq[tag] += 1
@@ -159,8 +167,7 @@ class PeerExchange:
         a.ld_dst = width
         a.flags = self.flags
         a.wait_ns = self.wait_ns
-        L.call("tcc_halo_push", C.byref(a), C.c_void_p(stream.cuda_stream))
-        return self.seq[tag]
+        return a
 
     def wait(self, tag: int, seq: int, stream: torch.cuda.Stream):
         """``stream`` continues once every sender's rows of step ``seq`` arrived."""

@@ -13,7 +13,8 @@ from tcc_b200 import _lib
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CUDA_INC = "/usr/local/cuda/include"
 MIRRORS = [(_lib.Swtcf, "tcc_swtcf"), (_lib.Bcsr, "tcc_bcsr"), (_lib.Bcsc, "tcc_bcsc"),
-           (_lib.IpcHandle, "tcc_ipc_handle"), (_lib.HaloPushArgs, "tcc_halo_push_args")]
+           (_lib.IpcHandle, "tcc_ipc_handle"), (_lib.HaloPushArgs, "tcc_halo_push_args"),
+           (_lib.DistOperand, "tcc_dist_operand"), (_lib.DistStepArgs, "tcc_dist_step_args")]
 
 
 def test_ctypes_structs_match_the_header(tmp_path):

@@ -2,7 +2,9 @@
 result -- the forward pass, the pipelined pair the bench times (several steps,
 new operands each, so a halo buffer is reused only after its readers released
 it), and the transposed pass of a directed graph (partial rows returned to
-their owners) -- with the halo moved by the peer-memory transport and by NCCL.
+their owners) -- with the halo moved by the peer-memory transport (steps
+sequenced by the library's tcc_dist_step, and call by call from Python) and
+by NCCL.
 Spawns one process per visible GPU (2 or more); skipped otherwise."""
 import os
 import socket
@@ -25,6 +27,7 @@ def _free_port():
 
 
 def _worker(rank, world, port, transport, q):
+    transport, _, host_step = transport.partition("-")
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -50,6 +53,8 @@ def _worker(rank, world, port, transport, q):
                        rs_local=s[r0:r1].contiguous(), cs_global=s, tc_threshold=65,
                        transport=transport)
         assert dg.transport == transport
+        if host_step:
+            dg.host_step = host_step
         gen = torch.Generator(device=dev)
         gen.manual_seed(3)
         X = torch.randn((deg.numel(), 64), generator=gen, device=dev)  # same X on every rank
@@ -79,6 +84,8 @@ def _worker(rank, world, port, transport, q):
         ddg = DistGraph((drp[a0:a1 + 1] - drp[a0]).contiguous(),
                         dcol[drp[a0]:drp[a1]].contiguous(), db, rs_local=rsd[a0:a1].contiguous(),
                         cs_global=None, tc_threshold=65, transport=transport)
+        if host_step:
+            ddg.host_step = host_step
         Zd = ddg.spmm_t(Gm[a0:a1].contiguous())
         dfull = tiles.from_csr(drp, dcol, ddeg.numel(), ddeg.numel(), kind="bcsc")
         Zdref = tiles.bcsc_spmm_t(dfull, Gm, tc_threshold=65, rs=rsd)[a0:a1]
@@ -97,7 +104,7 @@ def _worker(rank, world, port, transport, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2+ GPUs")
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
+@pytest.mark.parametrize("transport", ["peer-native", "peer-python", "nccl"])
 def test_row_partitioned_spmm_matches_single_gpu(gpu, transport):
     world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
