@@ -56,6 +56,22 @@ def test_null_arguments_are_rejected_without_a_gpu(lib):
     assert lib.tcc_tiles_workspace_create(C.byref(ws), 10, 0, 10) == 1
     with pytest.raises(_lib.TccError):
         _lib.call("tcc_swtcf_spmm", None, None, None, 12, None)
+    # the partitioned step: no arguments, no operands, a missing tiling
+    assert lib.tcc_dist_step(None, None, None) == 1
+    a = _lib.DistStepArgs()
+    assert lib.tcc_dist_step(C.byref(a), None, None) == 1               # n_ops == 0
+    assert b"n_ops" in lib.tcc_last_error()
+    a.n_ops = 1
+    assert lib.tcc_dist_step(C.byref(a), None, None) == 1               # no local tiles
+    # the halo exchange: no arguments, a bad tag, step number 0
+    assert lib.tcc_halo_push(None, None) == 1
+    h = _lib.HaloPushArgs()
+    h.world, h.rank, h.tag, h.seq, h.width = 2, 0, 9, 1, 4
+    assert lib.tcc_halo_push(C.byref(h), None) == 1
+    h.tag, h.seq = 0, 0
+    assert lib.tcc_halo_push(C.byref(h), None) == 1
+    assert lib.tcc_halo_wait(None, 0, 1, 1, 1000, None) == 1
+    assert lib.tcc_peer_alloc(0, C.byref(C.c_void_p()), C.byref(_lib.IpcHandle())) == 1
 
 
 def test_reference_build_exports_harness():
